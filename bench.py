@@ -1,0 +1,374 @@
+"""Benchmark of the B200 PISA attention call (BASELINE.json metric).
+
+Workload: Anima PISA HYD spatial self-attention,
+BF16 q/k/v [B=2,H=16,T=9216,D=128] as BHTD views of raster [B,T,H,D]
+storage, 23 of 144 exact KV blocks per query block.  One step = one
+``b200_pisa.forward_spatial_bhtd`` call over the whole batch (statistics,
+routing, fused exact + tail + correction attention, raster output).
+
+Multi-GPU (torchrun, one process per GPU): weak scaling -- every rank runs the
+full config-3 call on its own (batch, head) set; no collective on the data
+path.  Timing: W untimed warm-ups, then K steps between a barrier +
+synchronize on both sides, CUDA events on the launching stream, max over
+ranks.  The inputs (226 MB of q/k/v) exceed the 126 MB L2, so no extra flush.
+
+``--impl reference`` times the reference's PyTorch HYD path restated on the
+host CPU (oracle/pisa_oracle.py) on a bounded sample and reports the same
+metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "comfyui-rdna35-attention_b200"))
+
+B, H, T, D = 2, 16, 9216, 128
+NB = T // 64
+EXACT = 23
+METRIC = "PISA attn call ms & dense-equiv TFLOP/s, B=2 H=16 T=9216 D=128 bf16"
+UNIT = "dense-equiv TFLOP/s"
+DENSE_FLOP = 4.0 * B * H * T * T * D                     # 1391.6 GFLOP per call
+EXACT_FLOP = 4.0 * B * H * NB * EXACT * 64 * 64 * D       # 222.3 GFLOP
+TAIL_FLOP = 4.0 * B * H * T * NB * D                      # 21.7 GFLOP (q.kc and p.vc)
+CORR_FLOP = 2.0 * B * H * T * D * D                       # 9.66 GFLOP
+STATS_BYTES = 3 * B * H * T * D * 2                       # q/k/v read once
+CONFIG = {
+    "workload": "anima_pisa_hyd_spatial",
+    "batch": B, "heads": H, "tokens": T, "head_dim": D, "exact_blocks": EXACT, "blocks": NB,
+    "layout": "BHTD views of raster [B,T,H,D]; output [B,T,H*D]",
+    "l2": "inputs 226 MB > 126 MB L2 (no flush)",
+}
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm": data["hbm_gbs"], "bf16": data["bf16_tflops"], "bf16_sustained": data.get("bf16_tflops_sustained"),
+                "source": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = pathlib.Path(os.environ.get("TMPDIR", "/tmp")) / f"b2_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def _inputs(device, seed):
+    import pisa_oracle
+
+    q, k, v = pisa_oracle.anima_inputs(batch=B, heads=H, seed=seed)
+    return q, k, v
+
+
+def _timed(fn, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def run_b200(args) -> None:
+    world, rank, local = _dist()
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import b200_pisa
+    from b200_pisa import _lib
+
+    b200_pisa.prepare(local)
+    q_cpu, k_cpu, v_cpu = _inputs(device, seed=rank)
+    # raster BTHD storage on the host (pinned), BHTD views on the device
+    host = [x.permute(0, 2, 1, 3).contiguous().pin_memory() for x in (q_cpu, k_cpu, v_cpu)]
+    dev = [h.to(device).permute(0, 2, 1, 3) for h in host]
+    q, k, v = dev
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        return b200_pisa.forward_spatial_bhtd(q, k, v, exact_blocks=EXACT)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    with ClockSampler(local) as clocks:
+        barrier()
+        ms = _timed(step, args.steps, stream)
+        barrier()
+    clock_info = clocks.summary()
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    value = world * DENSE_FLOP / (ms * 1e-3) / 1e12
+
+    # ---- end to end through the public API: pinned host q/k/v -> device,
+    # call, output -> pinned host, all inside the timed region
+    out_host = torch.empty((B, T, H * D), dtype=torch.bfloat16).pin_memory()
+    dev_bthd = [torch.empty_like(h, device=device) for h in host]
+
+    def e2e_step():
+        for d_, h_ in zip(dev_bthd, host):
+            d_.copy_(h_, non_blocking=True)
+        out = b200_pisa.forward_spatial_bhtd(*(x.permute(0, 2, 1, 3) for x in dev_bthd), exact_blocks=EXACT)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e2e_ms = _timed(e2e_step, max(2, args.steps // 2), stream)
+    barrier()
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    h2d = sum(h.numel() * h.element_size() for h in host)
+    d2h = out_host.numel() * out_host.element_size()
+
+    # ---- component timing (dominant kernels, separate entry points)
+    comp = component_times(b200_pisa, _lib, q, k, v, device, stream, args.steps)
+
+    peaks = _peaks()
+    attn_flop = EXACT_FLOP + TAIL_FLOP + CORR_FLOP
+    achieved = attn_flop / (comp["attention_ms"] * 1e-3) / 1e12
+    roofline = {
+        "kernel": "attn_kernel (fused exact + tail + correction)",
+        "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16"], "unit": "TFLOP/s",
+        "frac": round(achieved / peaks["bf16"], 4), "peak_source": peaks["source"] + " bf16 burst",
+        "traffic": args.traffic,
+        "stats_kernel": {
+            "bound": "hbm", "achieved": round(STATS_BYTES / (comp["stats_ms"] * 1e-3) / 1e9, 1),
+            "peak": peaks["hbm"], "unit": "GB/s",
+            "frac": round(STATS_BYTES / (comp["stats_ms"] * 1e-3) / 1e9 / peaks["hbm"], 4),
+        },
+        "component_ms": comp,
+    }
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) + per-tile N(0,0.5) offsets)",
+            "config": CONFIG, "clocks": clock_info,
+            "e2e": {"value": round(world * DENSE_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT,
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 5 * args.steps,
+            "roofline": roofline,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_heads)
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def component_times(b200_pisa, _lib, q, k, v, device, stream, steps):
+    """Time the statistics kernel and the fused attention kernel separately
+    through their own C-ABI entry points (same buffers as the full call)."""
+    import ctypes
+
+    from b200_pisa import LIB, check
+
+    bh = B * H
+    grid = dict(order=_lib.ORDER_TILED8, grid=(96, 96))
+    qv, kv, vv = (_lib.view(x, **grid) for x in (q, k, v))
+    out = torch.empty((B, T, H * D), device=device, dtype=torch.bfloat16)
+    ov = _lib.view(out.view(B, T, H, D).permute(0, 2, 1, 3), **grid)
+    qc = torch.empty((bh, NB, D), device=device, dtype=torch.bfloat16)
+    kc = torch.empty((bh, NB, D), device=device, dtype=torch.float32)
+    vc = torch.empty((bh, NB, D), device=device, dtype=torch.bfloat16)
+    hs = torch.empty((bh, D, D), device=device, dtype=torch.float32)
+    hn = torch.empty((bh, NB), device=device, dtype=torch.float32)
+    h16 = torch.empty((bh, D, D), device=device, dtype=torch.bfloat16)
+    ws = torch.empty(int(LIB.b2_stats_workspace_bytes(bh, T, D)), device=device, dtype=torch.uint8)
+    idx = torch.empty((bh, NB, EXACT), device=device, dtype=torch.int32)
+    sel = torch.empty((bh, NB, (NB + 31) // 32), device=device, dtype=torch.int32)
+    st = stream.cuda_stream
+    scale = 1.0 / math.sqrt(D)
+
+    def stats():
+        check(LIB.b2_pisa_block_stats(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), _lib.STATS_HYD,
+                                      qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), hs.data_ptr(), hn.data_ptr(),
+                                      h16.data_ptr(), ws.data_ptr(), st))
+
+    def route():
+        check(LIB.b2_pisa_route(qc.data_ptr(), _lib.B2_BF16, kc.data_ptr(), _lib.B2_BF16, hn.data_ptr(), bh, NB, D,
+                                EXACT, scale, -2, idx.data_ptr(), sel.data_ptr(), st))
+
+    kc16 = kc.to(torch.bfloat16)
+
+    def attn():
+        check(LIB.b2_pisa_attention(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(ov),
+                                    idx.data_ptr(), EXACT, sel.data_ptr(), kc16.data_ptr(), vc.data_ptr(),
+                                    h16.data_ptr(), scale, None, st))
+
+    stats()
+    route()
+    kc16.copy_(kc.to(torch.bfloat16))
+    for fn in (stats, route, attn):
+        fn()
+    torch.cuda.synchronize(device)
+    return {"stats_ms": round(_timed(stats, steps, stream), 4), "route_ms": round(_timed(route, steps, stream), 4),
+            "attention_ms": round(_timed(attn, steps, stream), 4)}
+
+
+def cpu_baseline(heads: int) -> dict:
+    """The oracle (restated reference PyTorch HYD path) on host cores, on a
+    bounded sample of `heads` (batch, head) pairs at full T, scaled to the
+    metric for the full 32-head call."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pisa_oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    q, k, v = pisa_oracle.anima_inputs(batch=1, heads=heads, seed=0)
+    t0 = time.perf_counter()
+    pisa_oracle.hyd_forward_spatial(q, k, v, EXACT)
+    sec = time.perf_counter() - t0
+    call_sec = sec * (B * H) / heads
+    return {"value": round(DENSE_FLOP / call_sec / 1e12, 5), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{heads} of {B * H} (batch, head) pairs at T=9216, scaled x{B * H // heads}",
+            "ms_per_call_extrapolated": round(call_sec * 1e3, 1)}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pisa_oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    heads = args.cpu_heads
+    q, k, v = pisa_oracle.anima_inputs(batch=1, heads=heads, seed=0)
+    for _ in range(args.warmup):
+        pisa_oracle.hyd_forward_spatial(q, k, v, EXACT)
+    samples = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        pisa_oracle.hyd_forward_spatial(q, k, v, EXACT)
+        samples.append(time.perf_counter() - t0)
+    call_ms = statistics.median(samples) * 1e3 * (B * H) / heads
+    value = DENSE_FLOP / (call_ms * 1e-3) / 1e12
+    sample = f"{heads} of {B * H} (batch, head) pairs at T=9216 per step, scaled x{B * H // heads}"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(call_ms, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": CONFIG,
+        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    parser.add_argument("--cpu-heads", type=int, default=1)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--traffic", type=float, default=None,
+                        help="dram bytes per attention launch from an ncu capture (reported as roofline.traffic)")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

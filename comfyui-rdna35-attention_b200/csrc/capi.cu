@@ -1,0 +1,388 @@
+// C ABI entry points: argument validation (the TORCH_CHECK ladders of
+// native/rdna35_pisa_ck/csrc/pisa_kernels.cu:563-773 restated as status
+// codes), workspace carving and launch orchestration.  No entry point
+// allocates device memory or synchronises the stream.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "kernels.h"
+
+
+using namespace b2;
+
+namespace {
+
+thread_local char g_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(B2_ERR_CUDA, "%s failed: %s", what, cudaGetErrorString(err));
+}
+
+int ok() {
+  g_error[0] = '\0';
+  return B2_OK;
+}
+
+int esize_of(int dtype) { return dtype == B2_F32 ? 4 : 2; }
+
+// A view is usable by the 16-byte row kernels when every row start is
+// 16-byte aligned and the head dimension spans whole 16-byte vectors.
+int check_view(const b2_view* v, const char* name) {
+  if (v == nullptr) return fail(B2_ERR_INVALID, "%s view is NULL", name);
+  if (v->base == nullptr) return fail(B2_ERR_INVALID, "%s has a NULL base pointer", name);
+  if (v->batch <= 0 || v->heads <= 0 || v->tokens <= 0 || v->head_dim <= 0)
+    return fail(B2_ERR_INVALID, "%s requires positive B, H, T and D", name);
+  if (v->dtype != B2_BF16 && v->dtype != B2_F16 && v->dtype != B2_F32)
+    return fail(B2_ERR_INVALID, "%s has an unknown dtype %d", name, v->dtype);
+  const int es = esize_of(v->dtype);
+  if ((int64_t(v->head_dim) * es) % 16 != 0)
+    return fail(B2_ERR_INVALID, "%s head_dim*element size must be a multiple of 16 bytes", name);
+  if (reinterpret_cast<uintptr_t>(v->base) % 16 != 0) return fail(B2_ERR_INVALID, "%s must be 16-byte aligned", name);
+  if ((v->stride_b * es) % 16 || (v->stride_h * es) % 16 || (v->stride_t * es) % 16)
+    return fail(B2_ERR_INVALID, "%s strides must be multiples of 16 bytes", name);
+  if (v->order == B2_ORDER_TILED8) {
+    if (v->grid_h <= 0 || v->grid_w <= 0 || v->grid_h % 8 || v->grid_w % 8)
+      return fail(B2_ERR_INVALID, "%s tiled order requires grid sides divisible by 8", name);
+    const int64_t frame = int64_t(v->grid_h) * v->grid_w;
+    if (v->tokens % frame) return fail(B2_ERR_INVALID, "%s tokens must be a multiple of grid_h*grid_w", name);
+  } else if (v->order != B2_ORDER_LINEAR) {
+    return fail(B2_ERR_INVALID, "%s has an unknown token order %d", name, v->order);
+  }
+  return B2_OK;
+}
+
+bool same_bht(const b2_view* a, const b2_view* b) {
+  return a->batch == b->batch && a->heads == b->heads && a->tokens == b->tokens && a->head_dim == b->head_dim;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct PisaWorkspace {
+  void* qc;
+  float* kc;
+  void* vstat;
+  float* hsum;
+  void* h16;
+  float* hnorm;
+  void* kc16;
+  void* vc16;
+  int32_t* indices;
+  uint32_t* sel;
+  float* partial;
+  size_t total;
+};
+
+PisaWorkspace carve(char* base, int bh, int tokens, int dim, int k) {
+  const int nb = (tokens + kBlock - 1) / kBlock;
+  const int words = (nb + 31) / 32;
+  PisaWorkspace w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off += align256(bytes);
+    return p;
+  };
+  const size_t cent = size_t(bh) * nb * dim;
+  w.qc = take(cent * 4);
+  w.kc = reinterpret_cast<float*>(take(cent * 4));
+  w.vstat = take(cent * 4);
+  w.hsum = reinterpret_cast<float*>(take(size_t(bh) * dim * dim * 4));
+  w.h16 = take(size_t(bh) * dim * dim * 2);
+  w.hnorm = reinterpret_cast<float*>(take(size_t(bh) * nb * 4));
+  w.kc16 = take(cent * 2);
+  w.vc16 = take(cent * 2);
+  w.indices = reinterpret_cast<int32_t*>(take(size_t(bh) * nb * (k > 0 ? k : 1) * 4));
+  w.sel = reinterpret_cast<uint32_t*>(take(size_t(bh) * nb * words * 4));
+  w.partial = reinterpret_cast<float*>(take(static_cast<size_t>(stats_partial_bytes(bh, nb))));
+  w.total = off;
+  return w;
+}
+
+AttnParams base_params(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* o, float scale) {
+  AttnParams p{};
+  p.q = make_rows(*q);
+  p.k = make_rows(*k);
+  p.v = make_rows(*v);
+  p.o = make_rows(*o);
+  p.tq = q->tokens;
+  p.tk = k->tokens;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  return p;
+}
+
+int check_qkv_o(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* o, bool same_tokens) {
+  int rc;
+  if ((rc = check_view(q, "q")) || (rc = check_view(k, "k")) || (rc = check_view(v, "v")) ||
+      (rc = check_view(o, "out")))
+    return rc;
+  if (!same_bht(k, v)) return fail(B2_ERR_INVALID, "k and v must have matching [B,H,T,D]");
+  if (q->batch != k->batch || q->heads != k->heads || q->head_dim != k->head_dim)
+    return fail(B2_ERR_INVALID, "q and k must share B, H and D");
+  if (same_tokens && q->tokens != k->tokens) return fail(B2_ERR_INVALID, "self-attention requires Tq == Tk");
+  if (!same_bht(q, o)) return fail(B2_ERR_INVALID, "out must have q's [B,H,T,D]");
+  if (q->dtype != k->dtype || q->dtype != v->dtype || q->dtype != o->dtype)
+    return fail(B2_ERR_INVALID, "q, k, v and out must share one dtype");
+  return B2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* b2_last_error(void) { return g_error; }
+
+int b2_api_version(void) { return B200ATTN_API_VERSION; }
+
+int b2_build_info(char* buffer, int64_t capacity) {
+  if (buffer == nullptr || capacity <= 0) return fail(B2_ERR_INVALID, "build_info buffer is empty");
+  snprintf(buffer, static_cast<size_t>(capacity),
+           "api=%d;architecture=sm_100a;cuda_build_version=%d;implementation=b200_pisa_fused;block_size=64;"
+           "head_dim=128;max_blocks=1024",
+           B200ATTN_API_VERSION, CUDART_VERSION);
+  return ok();
+}
+
+int b2_check_device(int device_index) {
+  cudaDeviceProp prop;
+  const cudaError_t err = cudaGetDeviceProperties(&prop, device_index);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDeviceProperties");
+  if (prop.major != 10) return fail(B2_ERR_DEVICE, "sm_100 (B200) is required, device %d is sm_%d%d", device_index,
+                                    prop.major, prop.minor);
+  return ok();
+}
+
+int64_t b2_stats_workspace_bytes(int32_t batch_heads, int32_t tokens, int32_t head_dim) {
+  if (batch_heads <= 0 || tokens <= 0 || head_dim != 128) return -1;
+  return stats_partial_bytes(batch_heads, (tokens + kBlock - 1) / kBlock);
+}
+
+int b2_pisa_block_stats(const b2_view* q, const b2_view* k, const b2_view* v, int32_t mode, void* q_centroids,
+                        float* k_centroids, void* v_stats, float* h_sum, float* h_norm, void* h_bf16,
+                        void* workspace, void* stream) {
+  int rc;
+  if ((rc = check_view(q, "q")) || (rc = check_view(k, "k")) || (rc = check_view(v, "v"))) return rc;
+  if (!same_bht(q, k) || !same_bht(q, v)) return fail(B2_ERR_INVALID, "PISA statistics expect matching q/k/v");
+  if (q->dtype != k->dtype || q->dtype != v->dtype) return fail(B2_ERR_INVALID, "q, k and v must share one dtype");
+  if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA statistics support bfloat16 and float16");
+  if (q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "PISA statistics require D=128");
+  if (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC) return fail(B2_ERR_INVALID, "unknown statistics mode");
+  if (!q_centroids || !k_centroids || !v_stats || !h_sum || !workspace)
+    return fail(B2_ERR_INVALID, "PISA statistics outputs and workspace must be non-NULL");
+  const int bh = q->batch * q->heads;
+  const int nb = (q->tokens + kBlock - 1) / kBlock;
+  const cudaError_t err =
+      launch_stats(make_rows(*q), make_rows(*k), make_rows(*v), q->dtype, mode, bh, nb, q_centroids, k_centroids,
+                   v_stats, h_sum, h_norm, h_bf16, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "PISA block statistics launch");
+  return ok();
+}
+
+int b2_pisa_route(const void* qc, int32_t qc_dtype, const float* kc, int32_t kc_round, const float* h_norm,
+                  int32_t batch_heads, int32_t blocks, int32_t head_dim, int32_t exact_blocks, float scale,
+                  int32_t sink_block, int32_t* indices, uint32_t* sel_bits, void* stream) {
+  if (!qc || !kc || !indices || !sel_bits) return fail(B2_ERR_INVALID, "routing pointers must be non-NULL");
+  if (batch_heads <= 0 || blocks <= 0 || head_dim <= 0) return fail(B2_ERR_INVALID, "routing sizes must be positive");
+  if (blocks > 1024) return fail(B2_ERR_UNSUPPORTED, "routing supports at most 1024 blocks");
+  if (exact_blocks < 0 || exact_blocks > blocks) return fail(B2_ERR_INVALID, "exact_blocks must be in [0,%d]", blocks);
+  if (sink_block != -2 && sink_block != -1 && sink_block != 0)
+    return fail(B2_ERR_INVALID, "sink_block must be None, -1, or 0.");
+  if (qc_dtype != B2_BF16 && qc_dtype != B2_F32) return fail(B2_ERR_INVALID, "routing centroids must be BF16 or FP32");
+  const cudaError_t err = launch_route(qc, qc_dtype, kc, kc_round, h_norm, batch_heads, blocks, head_dim,
+                                       exact_blocks, scale, sink_block, indices, sel_bits,
+                                       static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "PISA routing launch");
+  return ok();
+}
+
+int b2_pisa_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out,
+                      const int32_t* indices, int32_t exact_blocks, const uint32_t* sel_bits, const void* kc_bf16,
+                      const void* vc_bf16, const void* h_bf16, float scale, float* lse, void* stream) {
+  int rc = check_qkv_o(q, k, v, out, true);
+  if (rc) return rc;
+  if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA attention supports bfloat16 and float16");
+  if (q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "PISA attention requires D=128");
+  const int nb = (q->tokens + kBlock - 1) / kBlock;
+  if (exact_blocks < 0 || exact_blocks > nb) return fail(B2_ERR_INVALID, "exact_blocks must be in [0,%d]", nb);
+  if (exact_blocks > 0 && indices == nullptr) return fail(B2_ERR_INVALID, "indices are required");
+  if (kc_bf16 != nullptr && (vc_bf16 == nullptr || sel_bits == nullptr))
+    return fail(B2_ERR_INVALID, "the tail needs centroid values and selection bits");
+  AttnParams p = base_params(q, k, v, out, scale);
+  p.mode = 1;
+  p.indices = indices;
+  p.nsel = exact_blocks;
+  p.sel_bits = sel_bits;
+  p.nb = kc_bf16 ? nb : 0;
+  p.kc = kc_bf16;
+  p.vc = vc_bf16;
+  p.h = h_bf16;
+  p.corr_scale = scale / static_cast<float>(q->tokens);
+  p.lse = lse;
+  const cudaError_t err = launch_attn_mma(p, q->dtype, q->batch * q->heads, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "PISA attention launch");
+  return ok();
+}
+
+int64_t b2_pisa_workspace_bytes(int32_t batch_heads, int32_t tokens, int32_t head_dim, int32_t exact_blocks) {
+  if (batch_heads <= 0 || tokens <= 0 || head_dim != 128 || exact_blocks < 0) return -1;
+  return static_cast<int64_t>(carve(nullptr, batch_heads, tokens, head_dim, exact_blocks).total);
+}
+
+int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, int32_t exact_blocks,
+                    float scale, int32_t sink_block, int32_t stats_mode, int32_t first_order, void* workspace,
+                    void* stream) {
+  int rc = check_qkv_o(q, k, v, out, true);
+  if (rc) return rc;
+  if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA supports bfloat16 and float16");
+  if (q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "PISA requires D=128");
+  if (!(scale > 0.f) || !(scale < 3.4028235e38f))
+    return fail(B2_ERR_INVALID, "scale must be representable as a positive finite float32 value.");
+  const int nb = (q->tokens + kBlock - 1) / kBlock;
+  if (nb > 1024) return fail(B2_ERR_UNSUPPORTED, "PISA supports at most 1024 blocks");
+  if (exact_blocks < 0 || exact_blocks > nb) return fail(B2_ERR_INVALID, "exact_blocks must be in [0,%d].", nb);
+  if (sink_block != -2 && sink_block != -1 && sink_block != 0)
+    return fail(B2_ERR_INVALID, "sink_block must be None, -1, or 0.");
+  if (sink_block != -2 && exact_blocks == 0) return fail(B2_ERR_INVALID, "sink_block requires at least one exact block.");
+  if (stats_mode != B2_STATS_HYD && stats_mode != B2_STATS_GENERIC) return fail(B2_ERR_INVALID, "unknown stats mode");
+  if (stats_mode == B2_STATS_HYD && q->dtype != B2_BF16)
+    return fail(B2_ERR_UNSUPPORTED, "HYD PISA requires matching bfloat16 q/k/v.");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int bh = q->batch * q->heads;
+  cudaError_t err;
+  if (exact_blocks == nb) {
+    AttnParams p = base_params(q, k, v, out, scale);
+    p.mode = 0;
+    err = launch_attn_mma(p, q->dtype, bh, st);
+    if (err != cudaSuccess) return cuda_fail(err, "dense attention launch");
+    return ok();
+  }
+  if (workspace == nullptr) return fail(B2_ERR_INVALID, "workspace must be non-NULL");
+  PisaWorkspace w = carve(static_cast<char*>(workspace), bh, q->tokens, q->head_dim, exact_blocks);
+  const bool hyd = stats_mode == B2_STATS_HYD;
+  err = launch_stats(make_rows(*q), make_rows(*k), make_rows(*v), q->dtype, stats_mode, bh, nb, w.qc, w.kc, w.vstat,
+                     w.hsum, w.hnorm, w.h16, w.partial, st);
+  if (err != cudaSuccess) return cuda_fail(err, "PISA statistics launch");
+  err = launch_centroid_prep(w.kc, w.vstat, hyd ? 0 : 1, bh, nb, q->tokens, q->head_dim, q->dtype, w.kc16, w.vc16, st);
+  if (err != cudaSuccess) return cuda_fail(err, "PISA centroid preparation launch");
+  const int words = (nb + 31) / 32;
+  if (exact_blocks > 0) {
+    err = launch_route(w.qc, hyd ? B2_BF16 : B2_F32, w.kc, hyd ? B2_BF16 : B2_F32, hyd ? w.hnorm : nullptr, bh, nb,
+                       q->head_dim, exact_blocks, scale, hyd ? sink_block : -2, w.indices, w.sel, st);
+    if (err != cudaSuccess) return cuda_fail(err, "PISA routing launch");
+  } else {
+    err = cudaMemsetAsync(w.sel, 0, size_t(bh) * nb * words * 4, st);
+    if (err != cudaSuccess) return cuda_fail(err, "selection reset");
+  }
+  AttnParams p = base_params(q, k, v, out, scale);
+  p.mode = 1;
+  p.indices = w.indices;
+  p.nsel = exact_blocks;
+  p.sel_bits = w.sel;
+  p.nb = nb;
+  p.kc = w.kc16;
+  p.vc = w.vc16;
+  p.h = first_order ? w.h16 : nullptr;
+  p.corr_scale = scale / static_cast<float>(q->tokens);
+  err = launch_attn_mma(p, q->dtype, bh, st);
+  if (err != cudaSuccess) return cuda_fail(err, "PISA attention launch");
+  return ok();
+}
+
+int b2_full_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, float scale,
+                      float* lse, void* stream) {
+  int rc = check_qkv_o(q, k, v, out, false);
+  if (rc) return rc;
+  if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "full attention supports float16 and bfloat16");
+  if (q->head_dim != 64 && q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "full attention supports D in {64,128}");
+  AttnParams p = base_params(q, k, v, out, scale);
+  p.mode = 0;
+  p.lse = lse;
+  const cudaError_t err = launch_attn_mma(p, q->dtype, q->batch * q->heads, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "full attention launch");
+  return ok();
+}
+
+int b2_fixed_block_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, float scale,
+                             int32_t causal, void* stream) {
+  int rc = check_qkv_o(q, k, v, out, true);
+  if (rc) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t err;
+  if (q->dtype == B2_F32) {
+    if (q->head_dim > 128) return fail(B2_ERR_UNSUPPORTED, "FP32 fixed-block attention supports D <= 128");
+    err = launch_fixed_f32(make_rows(*q), make_rows(*k), make_rows(*v), make_rows(*out), q->batch * q->heads, scale,
+                           causal, st);
+  } else {
+    if (q->head_dim != 32 && q->head_dim != 64 && q->head_dim != 128)
+      return fail(B2_ERR_UNSUPPORTED, "fixed-block attention supports D in {32,64,128}");
+    AttnParams p = base_params(q, k, v, out, scale);
+    p.mode = 2;
+    p.causal = causal ? 1 : 0;
+    err = launch_attn_mma(p, q->dtype, q->batch * q->heads, st);
+  }
+  if (err != cudaSuccess) return cuda_fail(err, "fixed-block attention launch");
+  return ok();
+}
+
+int b2_pack_rows(const b2_view* src, void* dst, void* stream) {
+  int rc = check_view(src, "src");
+  if (rc) return rc;
+  if (dst == nullptr || reinterpret_cast<uintptr_t>(dst) % 16) return fail(B2_ERR_INVALID, "dst must be 16-byte aligned");
+  const cudaError_t err = launch_pack_rows(make_rows(*src), src->batch * src->heads, dst, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "pack launch");
+  return ok();
+}
+
+int b2_unpack_rows(const void* src, const b2_view* dst, void* stream) {
+  int rc = check_view(dst, "dst");
+  if (rc) return rc;
+  if (src == nullptr || reinterpret_cast<uintptr_t>(src) % 16) return fail(B2_ERR_INVALID, "src must be 16-byte aligned");
+  const cudaError_t err = launch_unpack_rows(src, make_rows(*dst), dst->batch * dst->heads, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "unpack launch");
+  return ok();
+}
+
+int b2_merge_epilogue(const void* exact, const float* exact_lse, const void* approx, const float* approx_lse,
+                      const float* correction, const b2_view* dst, void* stream) {
+  int rc = check_view(dst, "dst");
+  if (rc) return rc;
+  if (dst->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "merge epilogue writes bfloat16 or float16");
+  if (!exact || !exact_lse || !approx || !approx_lse || !correction)
+    return fail(B2_ERR_INVALID, "merge inputs must be non-NULL");
+  for (const void* ptr : {exact, approx, static_cast<const void*>(correction)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return fail(B2_ERR_INVALID, "merge inputs must be 16-byte aligned");
+  const cudaError_t err = launch_merge(exact, exact_lse, approx, approx_lse, correction, make_rows(*dst), dst->dtype,
+                                       dst->batch * dst->heads, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "merge epilogue launch");
+  return ok();
+}
+
+int b2_h3_pack(const b2_view* views, int32_t n, void* dst, void* stream) {
+  if (views == nullptr || n < 1 || n > 3) return fail(B2_ERR_INVALID, "h3 pack takes 1..3 views");
+  if (dst == nullptr || reinterpret_cast<uintptr_t>(dst) % 16) return fail(B2_ERR_INVALID, "dst must be 16-byte aligned");
+  for (int i = 0; i < n; ++i) {
+    int rc = check_view(&views[i], "h3 view");
+    if (rc) return rc;
+    if (!same_bht(&views[0], &views[i]) || views[i].dtype != views[0].dtype)
+      return fail(B2_ERR_INVALID, "h3 views must share shape and dtype");
+  }
+  const int64_t bytes = int64_t(views[0].batch) * views[0].heads * views[0].tokens * views[0].head_dim *
+                        esize_of(views[0].dtype);
+  for (int i = 0; i < n; ++i) {
+    const cudaError_t err = launch_pack_rows(make_rows(views[i]), views[i].batch * views[i].heads,
+                                             static_cast<char*>(dst) + i * bytes, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "h3 pack launch");
+  }
+  return ok();
+}
+
+}  // extern "C"

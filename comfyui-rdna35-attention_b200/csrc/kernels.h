@@ -1,0 +1,40 @@
+// Internal launch interface shared by the C ABI layer and the kernels.
+#pragma once
+#include "common.cuh"
+
+namespace b2 {
+// Parameters of the fused attention kernel (see attn_mma.cu).
+struct AttnParams {
+  Rows q, k, v, o;
+  int tq, tk;
+  int mode;
+  const int32_t* indices;
+  int nsel;
+  const uint32_t* sel_bits;
+  int nb;
+  const void* kc;
+  const void* vc;
+  const void* h;
+  float scale;
+  float scale_log2;
+  float corr_scale;
+  float* lse;
+  int causal;
+};
+cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype, int mode, int batch_heads,
+                         int blocks, void* q_centroids, float* k_centroids, void* v_stats, float* h_sum,
+                         float* h_norm, void* h_half, float* partial, cudaStream_t stream);
+int64_t stats_partial_bytes(int batch_heads, int blocks);
+cudaError_t launch_route(const void* qc, int qc_dtype, const float* kc, int kc_round, const float* h_norm,
+                         int batch_heads, int blocks, int dim, int k, float scale, int sink, int32_t* indices,
+                         uint32_t* sel_bits, cudaStream_t stream);
+cudaError_t launch_attn_mma(const AttnParams& p, int dtype, int batch_heads, cudaStream_t stream);
+cudaError_t launch_pack_rows(const Rows& src, int batch_heads, void* dst, cudaStream_t stream);
+cudaError_t launch_unpack_rows(const void* src, const Rows& dst, int batch_heads, cudaStream_t stream);
+cudaError_t launch_merge(const void* exact, const float* exact_lse, const void* approx, const float* approx_lse,
+                         const float* corr, const Rows& dst, int dtype, int batch_heads, cudaStream_t stream);
+cudaError_t launch_centroid_prep(const float* kc, const void* vstat, int vstat_is_sum, int batch_heads, int blocks,
+                                 int tokens, int dim, int dtype, void* kc16, void* vc16, cudaStream_t stream);
+cudaError_t launch_fixed_f32(const Rows& q, const Rows& k, const Rows& v, const Rows& o, int batch_heads,
+                             float scale, int causal, cudaStream_t stream);
+}  // namespace b2

@@ -1,0 +1,165 @@
+/*
+ * b200attn.h -- C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and a
+ * cudaStream_t passed as void*, launches asynchronously on that stream and
+ * returns 0 on success or a B2_ERR_* code.  b2_last_error() returns a
+ * thread-local message describing the most recent failure.  No entry point
+ * synchronises the stream or allocates device memory; callers own every
+ * buffer (outputs and the scratch workspace sized by b2_pisa_workspace_bytes).
+ *
+ * Reference interfaces replaced (paths inside the ComfyUI-RDNA35-Attention
+ * project):
+ *   native/rdna35_pisa_ck/csrc/pisa_kernels.cu:563-594  pisa_block_stats
+ *   native/rdna35_pisa_ck/csrc/pisa_kernels.cu:597-635  pisa_block_stats_hyd
+ *   native/rdna35_pisa_ck/csrc/pisa_kernels.cu:638-676  pisa_pack_spatial_qkv
+ *   native/rdna35_pisa_ck/csrc/pisa_kernels.cu:679-707  pisa_unpack_spatial_output
+ *   native/rdna35_pisa_ck/csrc/pisa_kernels.cu:710-773  pisa_fuse_spatial_epilogue
+ *   native/rdna35_pisa_ck/csrc/bindings.cpp:70-82       build_info
+ *   native/rdna35_pisa_ck/rdna35_pisa_ck/__init__.py:233-316 _forward_impl
+ *       (routing + FlexAttention exact/tail + correction GEMM + merge)
+ *   rdna35_block_attention/triton_kernel.py:53-100,200-244 fixed-block kernel
+ *   rdna35_block_attention/triton_kernel.py:113-197      full attention kernel
+ *   rdna35_block_attention/minimax_h3_gfx1151_attention.py:64-74 H3 pack
+ *   rdna35_block_attention/pisa_kernel.py:49-131         Triton PISA stats
+ */
+#ifndef B200ATTN_H
+#define B200ATTN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200ATTN_API_VERSION 7
+
+enum b2_status {
+  B2_OK = 0,
+  B2_ERR_INVALID = 1,      /* bad shape, stride, alignment or argument */
+  B2_ERR_UNSUPPORTED = 2,  /* valid request this build does not implement */
+  B2_ERR_CUDA = 3,         /* a CUDA runtime call or launch failed */
+  B2_ERR_DEVICE = 4        /* the current device is not sm_100 */
+};
+
+enum b2_dtype { B2_BF16 = 0, B2_F16 = 1, B2_F32 = 2 };
+
+/* Token order of a row view.  B2_ORDER_LINEAR: row t is token t.
+ * B2_ORDER_TILED8: row t walks 8x8 spatial tiles of a grid_h x grid_w raster
+ * (per frame, frames = tokens / (grid_h*grid_w)); within a tile rows go
+ * row-major.  This is the block-major order of pisa_kernels.cu:55-64
+ * (ordered_to_raster) and generic_pisa.py:17-52. */
+enum b2_order { B2_ORDER_LINEAR = 0, B2_ORDER_TILED8 = 1 };
+
+/* A [B,H,T,D] tensor view addressed by element strides.  Row (b,h,t) starts
+ * at base + b*stride_b + h*stride_h + map(t)*stride_t, where map is given by
+ * order/grid_h/grid_w; the D elements of a row are contiguous. */
+typedef struct b2_view {
+  void* base;
+  int64_t stride_b, stride_h, stride_t;
+  int32_t batch, heads, tokens, head_dim;
+  int32_t dtype;   /* enum b2_dtype */
+  int32_t order;   /* enum b2_order */
+  int32_t grid_h, grid_w;
+} b2_view;
+
+/* Statistic semantics. B2_STATS_HYD follows pisa_kernels.cu:167-244 (sums
+ * times 1/len, BF16 q/v centroids, FP32-centred K).  B2_STATS_GENERIC follows
+ * generic_pisa.py:106-138 + pisa_kernel.py:49-84 (sums divided by len, FP32
+ * centroids, BF16-rounded centred K, V sums). */
+enum b2_stats_mode { B2_STATS_HYD = 0, B2_STATS_GENERIC = 1 };
+
+const char* b2_last_error(void);
+int b2_api_version(void);
+/* Writes a NUL-terminated "key=value;..." build description. */
+int b2_build_info(char* buffer, int64_t capacity);
+/* Fails with B2_ERR_DEVICE unless device_index is an sm_100 GPU. */
+int b2_check_device(int device_index);
+
+/* ---- PISA block statistics (pisa_kernels.cu:597-635, pisa_kernel.py:90-131).
+ * q,k,v: [BH,T,D] views (D=128).  Outputs are contiguous:
+ *   q_centroids [BH,nb,D] (BF16 for HYD, FP32 for GENERIC),
+ *   k_centroids [BH,nb,D] FP32,
+ *   v_stats     [BH,nb,D] (HYD: BF16 means; GENERIC: FP32 sums),
+ *   h_sum       [BH,D,D] FP32, h_norm [BH,nb] FP32 (may be NULL),
+ *   h_bf16      [BH,D,D] BF16 copy of h_sum (may be NULL).
+ * workspace: b2_stats_workspace_bytes() bytes of scratch. */
+int64_t b2_stats_workspace_bytes(int32_t batch_heads, int32_t tokens, int32_t head_dim);
+int b2_pisa_block_stats(const b2_view* q, const b2_view* k, const b2_view* v,
+                        int32_t mode, void* q_centroids, float* k_centroids,
+                        void* v_stats, float* h_sum, float* h_norm,
+                        void* h_bf16, void* workspace, void* stream);
+
+/* ---- HYD routing + top-k (rdna35_pisa_ck/__init__.py:258-269; generic
+ * routing without the h_norm bias: generic_pisa.py:172-184).
+ * scores[i,j] = dot(qc_i, kc_j)*scale (+ log(h_norm_j + 1e-5) when h_norm is
+ * not NULL); sink_block in {-2 (none), -1, 0} forces that column to +inf.
+ * qc: [BH,nb,D] (qc_dtype BF16 or FP32); kc: [BH,nb,D] FP32, rounded to the
+ * routing dtype kc_round (B2_BF16 rounds to BF16 first, B2_F32 keeps FP32).
+ * Writes indices [BH,nb,k] int32 sorted ascending and sel_bits
+ * [BH,nb,ceil(nb/32)] uint32 (bit j set when block j is exact). */
+int b2_pisa_route(const void* qc, int32_t qc_dtype, const float* kc,
+                  int32_t kc_round, const float* h_norm, int32_t batch_heads,
+                  int32_t blocks, int32_t head_dim, int32_t exact_blocks,
+                  float scale, int32_t sink_block, int32_t* indices,
+                  uint32_t* sel_bits, void* stream);
+
+/* ---- Fused PISA attention: exact block-sparse softmax attention over the
+ * selected KV blocks + centroid tail (logits q.kc*scale + log len, selected
+ * masked) + first-order correction q.H*scale/T weighted by the tail mass,
+ * merged in one online softmax (rdna35_pisa_ck/__init__.py:272-316,
+ * pisa_kernels.cu:296-340).  The output view may be tiled (raster write).
+ * kc_bf16/vc_bf16: [BH,nb,D] centroid rows in the input's 16-bit type
+ * (kc NULL: no tail); h_bf16 [BH,D,D] in the same type or NULL to skip the
+ * correction; lse: [BH,T] FP32 or NULL.  q/k/v/out share [B,H,T,D=128]. */
+int b2_pisa_attention(const b2_view* q, const b2_view* k, const b2_view* v,
+                      const b2_view* out, const int32_t* indices,
+                      int32_t exact_blocks, const uint32_t* sel_bits,
+                      const void* kc_bf16, const void* vc_bf16,
+                      const void* h_bf16, float scale, float* lse, void* stream);
+
+/* ---- Whole PISA forward in one call: stats, routing, fused attention.
+ * stats_mode B2_STATS_HYD: rdna35_pisa_ck forward / forward_spatial_bhtd
+ * (__init__.py:233-316); B2_STATS_GENERIC: generic_pisa_attention
+ * (generic_pisa.py:141-232, sink_block must be -2).  first_order=0 drops the
+ * correction term (generic_pisa.py:226-228).  exact_blocks == nb runs dense
+ * attention.  workspace: b2_pisa_workspace_bytes() bytes. */
+int64_t b2_pisa_workspace_bytes(int32_t batch_heads, int32_t tokens,
+                                int32_t head_dim, int32_t exact_blocks);
+int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v,
+                    const b2_view* out, int32_t exact_blocks, float scale,
+                    int32_t sink_block, int32_t stats_mode,
+                    int32_t first_order, void* workspace, void* stream);
+
+/* ---- Exact full attention (triton_kernel.py:113-197): out = softmax(q k^T
+ * scale) v over all Tk keys, no mask.  q: [B,H,Tq,D], k/v: [B,H,Tk,D]
+ * views, D in {64,128}, BF16 or FP16.  lse may be NULL. */
+int b2_full_attention(const b2_view* q, const b2_view* k, const b2_view* v,
+                      const b2_view* out, float scale, float* lse, void* stream);
+
+/* ---- Fixed 64-token block-diagonal attention (triton_kernel.py:53-100 and
+ * reference.py:159-200): each query block attends to its own key block.
+ * BF16/FP16 (D in {32,64,128}) or FP32 (D <= 128).  causal: 0/1. */
+int b2_fixed_block_attention(const b2_view* q, const b2_view* k,
+                             const b2_view* v, const b2_view* out, float scale,
+                             int32_t causal, void* stream);
+
+/* ---- Layout kernels. */
+/* pisa_kernels.cu:247-272: [B,H,T,D] tiled views -> contiguous [BH,T,D]. */
+int b2_pack_rows(const b2_view* src, void* dst, void* stream);
+/* pisa_kernels.cu:275-293: contiguous [BH,T,D] -> view (e.g. raster). */
+int b2_unpack_rows(const void* src, const b2_view* dst, void* stream);
+/* pisa_kernels.cu:296-340: LSE-weighted merge, block-major -> dst view.
+ * exact/approx: [BH,T,D] BF16, lses [BH,T] FP32, correction [BH,T,D] FP32. */
+int b2_merge_epilogue(const void* exact, const float* exact_lse,
+                      const void* approx, const float* approx_lse,
+                      const float* correction, const b2_view* dst,
+                      void* stream);
+/* minimax_h3_gfx1151_attention.py:64-74: copy n views (n in 1..3) of equal
+ * shape into one contiguous [n,B,H,T,D] allocation at dst. */
+int b2_h3_pack(const b2_view* views, int32_t n, void* dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200ATTN_H */
