@@ -307,7 +307,7 @@ def _native_block_stats(q, k, v, mode: int):
     bh, tokens, dim = q.shape
     blocks = (tokens + BLOCK_SIZE - 1) // BLOCK_SIZE
     _checked_device(q.device.index if q.device.index is not None else torch.cuda.current_device())
-    cent_dtype = q.dtype if mode == _lib.STATS_HYD else torch.float32
+    cent_dtype = torch.float32 if mode == _lib.STATS_GENERIC else q.dtype
     q_centroids = torch.empty((bh, blocks, dim), device=q.device, dtype=cent_dtype)
     k_centroids = torch.empty((bh, blocks, dim), device=q.device, dtype=torch.float32)
     v_stats = torch.empty((bh, blocks, dim), device=q.device, dtype=cent_dtype)
@@ -381,7 +381,7 @@ def _fuse_spatial_epilogue(exact_output, exact_lse, approximate_output, approxim
 
 
 def _c_block_stats(q, k, v):
-    out = _native_block_stats(q, k, v, _lib.STATS_HYD)
+    out = _native_block_stats(q, k, v, _lib.STATS_SCALED)
     return out[0], out[1], out[2]
 
 

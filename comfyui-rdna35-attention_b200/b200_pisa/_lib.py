@@ -25,7 +25,7 @@ B2_ERR_DEVICE = 4
 
 B2_BF16, B2_F16, B2_F32 = 0, 1, 2
 ORDER_LINEAR, ORDER_TILED8 = 0, 1
-STATS_HYD, STATS_GENERIC = 0, 1
+STATS_HYD, STATS_GENERIC, STATS_SCALED = 0, 1, 2
 
 _DTYPE_CODES = {torch.bfloat16: B2_BF16, torch.float16: B2_F16, torch.float32: B2_F32}
 

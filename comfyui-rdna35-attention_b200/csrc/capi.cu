@@ -175,7 +175,8 @@ int b2_pisa_block_stats(const b2_view* q, const b2_view* k, const b2_view* v, in
   if (q->dtype != k->dtype || q->dtype != v->dtype) return fail(B2_ERR_INVALID, "q, k and v must share one dtype");
   if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA statistics support bfloat16 and float16");
   if (q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "PISA statistics require D=128");
-  if (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC) return fail(B2_ERR_INVALID, "unknown statistics mode");
+  if (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC && mode != B2_STATS_SCALED)
+    return fail(B2_ERR_INVALID, "unknown statistics mode");
   if (!q_centroids || !k_centroids || !v_stats || !h_sum || !workspace)
     return fail(B2_ERR_INVALID, "PISA statistics outputs and workspace must be non-NULL");
   const int bh = q->batch * q->heads;

@@ -113,10 +113,17 @@ stats_kernel(Rows q, Rows k, Rows v, int blocks, int group, void* q_centroids, f
       const int col = task - tensor * kD;
       const T* tile = s.tiles[stage][tensor];
       float acc = 0.f;
-      for (int r = 0; r < len; ++r) acc += Cvt<T>::to_f(tile[r * kPad + col]);
-      if (MODE == B2_STATS_HYD) {
+      if (MODE == B2_STATS_SCALED) {
+        // each element times 1/len before the sum (pisa_kernels.cu:149-156)
         const float inv = 1.0f / static_cast<float>(len);
-        const float mean = acc * inv;
+        for (int r = 0; r < len; ++r) acc += Cvt<T>::to_f(tile[r * kPad + col]) * inv;
+      } else {
+        for (int r = 0; r < len; ++r) acc += Cvt<T>::to_f(tile[r * kPad + col]);
+      }
+      if (MODE != B2_STATS_GENERIC) {
+        const float inv = 1.0f / static_cast<float>(len);
+        const float mean = MODE == B2_STATS_SCALED ? acc : acc * inv;
+        (void)inv;
         if (tensor == 0) {
           static_cast<T*>(q_centroids)[out_base + col] = Cvt<T>::from_f(mean);
         } else if (tensor == 1) {
@@ -149,7 +156,7 @@ stats_kernel(Rows q, Rows k, Rows v, int blocks, int group, void* q_centroids, f
         if (r < len) centred = Cvt<T>::to_f(kt[r * kPad + c]) - s.kmean[c];
         const T hi = Cvt<T>::from_f(centred);
         s.kc_hi[r * kPad + c] = hi;
-        s.kc_lo[r * kPad + c] = Cvt<T>::from_f(MODE == B2_STATS_HYD ? centred - Cvt<T>::to_f(hi) : 0.f);
+        s.kc_lo[r * kPad + c] = Cvt<T>::from_f(MODE != B2_STATS_GENERIC ? centred - Cvt<T>::to_f(hi) : 0.f);
       }
     }
     __syncthreads();
@@ -168,7 +175,7 @@ stats_kernel(Rows q, Rows k, Rows v, int blocks, int group, void* q_centroids, f
         const int r = ks * 16 + (lane & 7) + ((mat >> 1) << 3);
         const int i = warp * 16 + ((mat & 1) << 3);
         ldsm_x4_trans(smem_u32(&s.kc_hi[r * kPad + i]), ahi[0], ahi[1], ahi[2], ahi[3]);
-        if (MODE == B2_STATS_HYD) ldsm_x4_trans(smem_u32(&s.kc_lo[r * kPad + i]), alo[0], alo[1], alo[2], alo[3]);
+        if (MODE != B2_STATS_GENERIC) ldsm_x4_trans(smem_u32(&s.kc_lo[r * kPad + i]), alo[0], alo[1], alo[2], alo[3]);
       }
 #pragma unroll
       for (int np = 0; np < 8; ++np) {
@@ -178,7 +185,7 @@ stats_kernel(Rows q, Rows k, Rows v, int blocks, int group, void* q_centroids, f
         ldsm_x4_trans(smem_u32(&vt[r * kPad + j]), b[0], b[1], b[2], b[3]);
         mma16816<T>(acc[2 * np], ahi, b[0], b[1]);
         mma16816<T>(acc[2 * np + 1], ahi, b[2], b[3]);
-        if (MODE == B2_STATS_HYD) {
+        if (MODE != B2_STATS_GENERIC) {
           mma16816<T>(acc[2 * np], alo, b[0], b[1]);
           mma16816<T>(acc[2 * np + 1], alo, b[2], b[3]);
         }
@@ -269,9 +276,11 @@ cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype,
   } while (0)
   if (dtype == B2_BF16) {
     if (mode == B2_STATS_HYD) B2_STATS_LAUNCH(__nv_bfloat16, B2_STATS_HYD);
+    else if (mode == B2_STATS_SCALED) B2_STATS_LAUNCH(__nv_bfloat16, B2_STATS_SCALED);
     else B2_STATS_LAUNCH(__nv_bfloat16, B2_STATS_GENERIC);
   } else {
     if (mode == B2_STATS_HYD) B2_STATS_LAUNCH(__half, B2_STATS_HYD);
+    else if (mode == B2_STATS_SCALED) B2_STATS_LAUNCH(__half, B2_STATS_SCALED);
     else B2_STATS_LAUNCH(__half, B2_STATS_GENERIC);
   }
 #undef B2_STATS_LAUNCH

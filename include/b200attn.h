@@ -67,7 +67,9 @@ typedef struct b2_view {
  * times 1/len, BF16 q/v centroids, FP32-centred K).  B2_STATS_GENERIC follows
  * generic_pisa.py:106-138 + pisa_kernel.py:49-84 (sums divided by len, FP32
  * centroids, BF16-rounded centred K, V sums). */
-enum b2_stats_mode { B2_STATS_HYD = 0, B2_STATS_GENERIC = 1 };
+enum b2_stats_mode { B2_STATS_HYD = 0, B2_STATS_GENERIC = 1, B2_STATS_SCALED = 2 };
+/* B2_STATS_SCALED: centroids only, each element times 1/len before the sum so
+ * extreme BF16 inputs cannot overflow (pisa_kernels.cu:130-164, block_stats). */
 
 const char* b2_last_error(void);
 int b2_api_version(void);
