@@ -176,6 +176,13 @@ def run_b200(args) -> None:
             dist.barrier()
         torch.cuda.synchronize(device)
 
+    if args.profile_only:
+        # launch-list / ncu mode: warm-ups + K plain steps, nothing else
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize(device)
+        print(json.dumps({"profile_only": True, "steps": args.steps, "warmup": args.warmup}))
+        return
     with ClockSampler(local) as clocks:
         barrier()
         ms = _timed(step, args.steps, stream)
@@ -359,6 +366,8 @@ def main() -> None:
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--cpu-heads", type=int, default=1)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--profile-only", action="store_true",
+                        help="run warm-ups and K plain steps only (for ncu launch lists / captures)")
     parser.add_argument("--traffic", type=float, default=None,
                         help="dram bytes per attention launch from an ncu capture (reported as roofline.traffic)")
     args = parser.parse_args()

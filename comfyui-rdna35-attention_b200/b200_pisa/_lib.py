@@ -57,6 +57,8 @@ _VIEW_P = ctypes.POINTER(View)
 
 SIGNATURES: dict[str, tuple] = {
     "b2_last_error": (ctypes.c_char_p, []),
+    "b2_last_kernel": (ctypes.c_char_p, []),
+    "b2_read_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
     "b2_api_version": (ctypes.c_int, []),
     "b2_build_info": (ctypes.c_int, [ctypes.c_char_p, _I64]),
     "b2_check_device": (ctypes.c_int, [ctypes.c_int]),
@@ -145,3 +147,15 @@ def build_info_string() -> str:
     buffer = ctypes.create_string_buffer(512)
     check(LIB.b2_build_info(buffer, len(buffer)))
     return buffer.value.decode()
+
+
+def last_kernel() -> str:
+    """Attention kernel this thread launched last ("tcgen05" or "mma_sync")."""
+    return LIB.b2_last_kernel().decode()
+
+
+def read_status() -> int:
+    """Read and clear the device status word (synchronises the device)."""
+    value = ctypes.c_int32(0)
+    check(LIB.b2_read_status(ctypes.byref(value)))
+    return value.value

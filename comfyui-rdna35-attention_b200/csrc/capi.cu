@@ -4,6 +4,7 @@
 // allocates device memory or synchronises the stream.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "kernels.h"
@@ -14,6 +15,34 @@ using namespace b2;
 namespace {
 
 thread_local char g_error[512] = "";
+thread_local const char* g_last_kernel = "none";
+
+// B200ATTN_KERNEL=mma forces the warp-level mma.sync attention kernel
+// (kept for layouts the TMA maps cannot express); default: tcgen05 kernel.
+bool umma_enabled() {
+  static const bool enabled = [] {
+    const char* env = getenv("B200ATTN_KERNEL");
+    return env == nullptr || strcmp(env, "mma") != 0;
+  }();
+  return enabled;
+}
+
+cudaError_t run_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* o, const AttnParams& p,
+                          cudaStream_t st) {
+  if (umma_enabled() && umma_supported(*q, *k, *v, *o)) {
+    bool launched = false;
+    int* status = device_status_ptr();
+    if (status != nullptr) {
+      const cudaError_t err = launch_attn_umma(*q, *k, *v, *o, p, status, st, &launched);
+      if (err != cudaSuccess || launched) {
+        g_last_kernel = "tcgen05";
+        return err;
+      }
+    }
+  }
+  g_last_kernel = "mma_sync";
+  return launch_attn_mma(p, q->dtype, q->batch * q->heads, st);
+}
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -141,6 +170,22 @@ extern "C" {
 
 const char* b2_last_error(void) { return g_error; }
 
+const char* b2_last_kernel(void) { return g_last_kernel; }
+
+int b2_read_status(int32_t* status) {
+  if (status == nullptr) return fail(B2_ERR_INVALID, "status pointer is NULL");
+  int* dev = device_status_ptr();
+  if (dev == nullptr) return fail(B2_ERR_CUDA, "device status word unavailable");
+  int value = 0;
+  cudaError_t err = cudaMemcpy(&value, dev, sizeof(int), cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) return cuda_fail(err, "status read");
+  const int zero = 0;
+  err = cudaMemcpy(dev, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  if (err != cudaSuccess) return cuda_fail(err, "status reset");
+  *status = value;
+  return ok();
+}
+
 int b2_api_version(void) { return B200ATTN_API_VERSION; }
 
 int b2_build_info(char* buffer, int64_t capacity) {
@@ -228,7 +273,7 @@ int b2_pisa_attention(const b2_view* q, const b2_view* k, const b2_view* v, cons
   p.h = h_bf16;
   p.corr_scale = scale / static_cast<float>(q->tokens);
   p.lse = lse;
-  const cudaError_t err = launch_attn_mma(p, q->dtype, q->batch * q->heads, static_cast<cudaStream_t>(stream));
+  const cudaError_t err = run_attention(q, k, v, out, p, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "PISA attention launch");
   return ok();
 }
@@ -262,7 +307,7 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
   if (exact_blocks == nb) {
     AttnParams p = base_params(q, k, v, out, scale);
     p.mode = 0;
-    err = launch_attn_mma(p, q->dtype, bh, st);
+    err = run_attention(q, k, v, out, p, st);
     if (err != cudaSuccess) return cuda_fail(err, "dense attention launch");
     return ok();
   }
@@ -293,7 +338,7 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
   p.vc = w.vc16;
   p.h = first_order ? w.h16 : nullptr;
   p.corr_scale = scale / static_cast<float>(q->tokens);
-  err = launch_attn_mma(p, q->dtype, bh, st);
+  err = run_attention(q, k, v, out, p, st);
   if (err != cudaSuccess) return cuda_fail(err, "PISA attention launch");
   return ok();
 }
@@ -307,7 +352,7 @@ int b2_full_attention(const b2_view* q, const b2_view* k, const b2_view* v, cons
   AttnParams p = base_params(q, k, v, out, scale);
   p.mode = 0;
   p.lse = lse;
-  const cudaError_t err = launch_attn_mma(p, q->dtype, q->batch * q->heads, static_cast<cudaStream_t>(stream));
+  const cudaError_t err = run_attention(q, k, v, out, p, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "full attention launch");
   return ok();
 }
@@ -328,7 +373,7 @@ int b2_fixed_block_attention(const b2_view* q, const b2_view* k, const b2_view* 
     AttnParams p = base_params(q, k, v, out, scale);
     p.mode = 2;
     p.causal = causal ? 1 : 0;
-    err = launch_attn_mma(p, q->dtype, q->batch * q->heads, st);
+    err = run_attention(q, k, v, out, p, st);
   }
   if (err != cudaSuccess) return cuda_fail(err, "fixed-block attention launch");
   return ok();

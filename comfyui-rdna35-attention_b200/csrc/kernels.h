@@ -21,6 +21,27 @@ struct AttnParams {
   float* lse;
   int causal;
 };
+// Arguments of the tcgen05 attention kernel (see attn_umma.cu).
+struct UmmaArgs {
+  int q_kind, kv_kind;  // 0 = linear 4D map, 1 = 8x8-tiled 5D map
+  int heads, tq, tk, nqb;
+  int frames, tiles_per_row, tiles_per_frame;
+  int mode;
+  const int32_t* indices;
+  int nsel;
+  const uint32_t* sel_bits;
+  int nb;
+  int has_corr;
+  float scale_log2, corr_scale, log2_last;
+  int causal;
+  Rows o;
+  float* lse;
+  int* status;
+};
+bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const b2_view& o);
+cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,
+                             const AttnParams& p, int* status, cudaStream_t stream, bool* launched);
+int* device_status_ptr();
 cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype, int mode, int batch_heads,
                          int blocks, void* q_centroids, float* k_centroids, void* v_stats, float* h_sum,
                          float* h_norm, void* h_half, float* partial, cudaStream_t stream);

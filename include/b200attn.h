@@ -72,6 +72,15 @@ enum b2_stats_mode { B2_STATS_HYD = 0, B2_STATS_GENERIC = 1, B2_STATS_SCALED = 2
  * extreme BF16 inputs cannot overflow (pisa_kernels.cu:130-164, block_stats). */
 
 const char* b2_last_error(void);
+/* Name of the attention kernel the calling thread launched last:
+ * "tcgen05" (TMA + tcgen05.mma + TMEM) or "mma_sync" (warp-level MMA, used
+ * for views the TMA maps cannot express or when B200ATTN_KERNEL=mma). */
+const char* b2_last_kernel(void);
+/* Synchronously reads and clears the current device's kernel status word:
+ * 0 when every kernel finished normally, else (1 << 8 | site) after a
+ * pipeline wait timed out (the kernel then ends early; outputs are invalid).
+ * This is the one entry point that synchronises (it copies 4 bytes). */
+int b2_read_status(int32_t* status);
 int b2_api_version(void);
 /* Writes a NUL-terminated "key=value;..." build description. */
 int b2_build_info(char* buffer, int64_t capacity);

@@ -106,8 +106,13 @@ def test_large_values_stay_finite(pisa):
 
 
 def test_spatial_forward_matches_oracle(pisa):
+    from b200_pisa import _lib
+
     q, k, v = oracle.anima_inputs(batch=1, heads=2, seed=3)
-    got = pisa.forward_spatial_bhtd(*(to_dev_bhtd(x) for x in (q, k, v)), exact_blocks=23).cpu().float()
+    got = pisa.forward_spatial_bhtd(*(to_dev_bhtd(x) for x in (q, k, v)), exact_blocks=23)
+    assert _lib.last_kernel() == "tcgen05"
+    assert _lib.read_status() == 0
+    got = got.cpu().float()
     exp, _ = oracle.hyd_forward_spatial(q, k, v, 23)
     assert got.shape == (1, 9216, 256)
     torch.testing.assert_close(got, exp.float(), **TOL)
