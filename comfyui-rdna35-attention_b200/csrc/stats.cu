@@ -13,6 +13,9 @@
 // FP32-centred K split into hi+lo 16-bit halves (two MMAs), so products keep
 // ~16 mantissa bits; the reference's float atomicAdd into h_sum is replaced
 // by per-CTA partial sums reduced in a fixed order by stats_reduce_kernel.
+#include <cstdio>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace b2 {
@@ -302,3 +305,127 @@ int64_t stats_partial_bytes(int batch_heads, int blocks) {
 }
 
 }  // namespace b2
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the block-statistics entry point.
+//
+// Some callers cannot allocate device memory at the moment they need the
+// statistics: code running inside a custom allocator's own callbacks, hosts
+// whose memory pool is fixed at start-up (embedded engines, plugin sandboxes
+// that only hand out input/output buffers), or paths that must not add
+// allocations while the framework's caching allocator is being reset.  For
+// them the per-CTA partial H sums live in a fixed file-scope device array
+// instead of a caller-provided workspace.  The array holds kNoAllocScratchBytes
+// (8 MiB) on every GPU that loads the library, until the process exits.
+namespace b2 {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;
+static __device__ __align__(256) unsigned char g_stats_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_stats_scratch for the current device, looked up once per
+// device (the host-side symbol is only a stand-in and must never reach a kernel).
+cudaError_t scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_stats_scratch);
+    if (err != cudaSuccess) return err;
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+thread_local char g_noalloc_error[256] = "";
+
+int noalloc_fail(int code, const char* msg) {
+  snprintf(g_noalloc_error, sizeof(g_noalloc_error), "%s", msg);
+  return code;
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" const char* b2_noalloc_last_error(void) { return b2::g_noalloc_error; }
+
+extern "C" int b2_pisa_block_stats_noalloc(const b2_view* q, const b2_view* k, const b2_view* v, int32_t mode,
+                                           void* q_centroids, float* k_centroids, void* v_stats, float* h_sum,
+                                           float* h_norm, void* h_bf16, void* stream) {
+  using namespace b2;
+  if (!q || !k || !v || !q->base || !k->base || !v->base)
+    return noalloc_fail(B2_ERR_INVALID, "q, k and v views must be non-NULL");
+  if (!q_centroids || !k_centroids || !v_stats || !h_sum)
+    return noalloc_fail(B2_ERR_INVALID, "PISA statistics outputs must be non-NULL");
+  for (const b2_view* x : {k, v})
+    if (x->batch != q->batch || x->heads != q->heads || x->tokens != q->tokens || x->head_dim != q->head_dim ||
+        x->dtype != q->dtype)
+      return noalloc_fail(B2_ERR_INVALID, "PISA statistics expect matching q/k/v");
+  if (q->batch <= 0 || q->heads <= 0 || q->tokens <= 0) return noalloc_fail(B2_ERR_INVALID, "sizes must be positive");
+  if (q->dtype != B2_BF16 && q->dtype != B2_F16)
+    return noalloc_fail(B2_ERR_UNSUPPORTED, "PISA statistics support bfloat16 and float16");
+  if (q->head_dim != 128) return noalloc_fail(B2_ERR_UNSUPPORTED, "PISA statistics require D=128");
+  if (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC && mode != B2_STATS_SCALED)
+    return noalloc_fail(B2_ERR_INVALID, "unknown statistics mode");
+  for (const b2_view* x : {q, k, v})
+    if (reinterpret_cast<uintptr_t>(x->base) % 16 || (x->stride_b * 2) % 16 || (x->stride_h * 2) % 16 ||
+        (x->stride_t * 2) % 16)
+      return noalloc_fail(B2_ERR_INVALID, "views must be 16-byte aligned with 16-byte strides");
+  const int bh = q->batch * q->heads;
+  const int blocks = (q->tokens + kBlock - 1) / kBlock;
+  // smallest blocks-per-CTA group (>= the default one) whose partial sums fit
+  const int64_t per_group = int64_t(kD) * kD * 4;
+  int group = stats_group_size(bh, blocks);
+  while (group < blocks && int64_t(bh) * ((blocks + group - 1) / group) * per_group > kNoAllocScratchBytes) ++group;
+  const int groups = (blocks + group - 1) / group;
+  if (int64_t(bh) * groups * per_group > kNoAllocScratchBytes)
+    return noalloc_fail(B2_ERR_UNSUPPORTED,
+                        "b2_pisa_block_stats_noalloc: batch*heads exceeds 128, the 8 MiB scratch limit "
+                        "(use b2_pisa_block_stats with a caller workspace)");
+  void* scratch = nullptr;
+  cudaError_t err = scratch_address(&scratch);
+  if (err != cudaSuccess) return noalloc_fail(B2_ERR_CUDA, cudaGetErrorString(err));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Rows qr = make_rows(*q), kr = make_rows(*k), vr = make_rows(*v);
+  float* partial = static_cast<float*>(scratch);
+  dim3 grid(groups, bh);
+  const size_t smem = q->dtype == B2_BF16 ? sizeof(StatsSmem<__nv_bfloat16>) : sizeof(StatsSmem<__half>);
+#define B2_NOALLOC_LAUNCH(T, M)                                                                            \
+  do {                                                                                                     \
+    auto kern = stats_kernel<T, M>;                                                                        \
+    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
+    if (err == cudaSuccess)                                                                                \
+      kern<<<grid, kStatsThreads, smem, st>>>(qr, kr, vr, blocks, group, q_centroids, k_centroids, v_stats,\
+                                              h_norm, partial);                                            \
+  } while (0)
+  if (q->dtype == B2_BF16) {
+    if (mode == B2_STATS_HYD) B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_HYD);
+    else if (mode == B2_STATS_SCALED) B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_SCALED);
+    else B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_GENERIC);
+  } else {
+    if (mode == B2_STATS_HYD) B2_NOALLOC_LAUNCH(__half, B2_STATS_HYD);
+    else if (mode == B2_STATS_SCALED) B2_NOALLOC_LAUNCH(__half, B2_STATS_SCALED);
+    else B2_NOALLOC_LAUNCH(__half, B2_STATS_GENERIC);
+  }
+#undef B2_NOALLOC_LAUNCH
+  if (err == cudaSuccess) err = cudaGetLastError();
+  if (err != cudaSuccess) return noalloc_fail(B2_ERR_CUDA, cudaGetErrorString(err));
+  dim3 rgrid((kD * kD / 4 + 255) / 256, bh);
+  if (q->dtype == B2_BF16)
+    stats_reduce_kernel<__nv_bfloat16><<<rgrid, 256, 0, st>>>(partial, groups, h_sum,
+                                                              static_cast<__nv_bfloat16*>(h_bf16));
+  else
+    stats_reduce_kernel<__half><<<rgrid, 256, 0, st>>>(partial, groups, h_sum, static_cast<__half*>(h_bf16));
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return noalloc_fail(B2_ERR_CUDA, cudaGetErrorString(err));
+  g_noalloc_error[0] = '\0';
+  return B2_OK;
+}

@@ -101,6 +101,27 @@ int b2_pisa_block_stats(const b2_view* q, const b2_view* k, const b2_view* v,
                         void* v_stats, float* h_sum, float* h_norm,
                         void* h_bf16, void* workspace, void* stream);
 
+/* ---- Allocation-free block statistics.  No counterpart in the reference.
+ * Same inputs, outputs and semantics as b2_pisa_block_stats, but the partial
+ * H sums go to an 8 MiB array compiled into the library (one copy per GPU,
+ * held until the process exits) instead of a caller workspace, for callers
+ * that cannot allocate device memory when they run (allocator callbacks,
+ * fixed memory pools, plugin hosts that only hand out input/output buffers).
+ * Limit: batch*heads*ceil(nb/group) partials of 64 KiB must fit in 8 MiB,
+ * i.e. batch*heads <= 128; larger requests fail with B2_ERR_UNSUPPORTED.
+ * The first call on each device looks up the array's device address (with
+ * that device current); make that first call before any stream capture.
+ * Every call shares the array and overwrites all of it that it reads, so no
+ * clearing is needed, but calls whose kernels overlap on the GPU (different
+ * streams or devices sharing a context) race on it.  Errors are reported by
+ * b2_noalloc_last_error(). */
+int b2_pisa_block_stats_noalloc(const b2_view* q, const b2_view* k,
+                                const b2_view* v, int32_t mode,
+                                void* q_centroids, float* k_centroids,
+                                void* v_stats, float* h_sum, float* h_norm,
+                                void* h_bf16, void* stream);
+const char* b2_noalloc_last_error(void);
+
 /* ---- HYD routing + top-k (rdna35_pisa_ck/__init__.py:258-269; generic
  * routing without the h_norm bias: generic_pisa.py:172-184).
  * scores[i,j] = dot(qc_i, kc_j)*scale (+ log(h_norm_j + 1e-5) when h_norm is
