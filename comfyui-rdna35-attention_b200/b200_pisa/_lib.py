@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_last_error": (ctypes.c_char_p, []),
     "b2_last_kernel": (ctypes.c_char_p, []),
     "b2_read_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
+    "b2_set_trace": (ctypes.c_int, [ctypes.c_void_p]),
     "b2_api_version": (ctypes.c_int, []),
     "b2_build_info": (ctypes.c_int, [ctypes.c_char_p, _I64]),
     "b2_check_device": (ctypes.c_int, [ctypes.c_int]),

@@ -13,19 +13,22 @@
 //   * fixed block (mode DIAG): each query block's own key block
 //     (triton_kernel.py:53-100, optional causal mask).
 //
-// Warp roles (192 threads):
+// Warp roles (320 threads, one CTA per SM):
 //   warp 0    TMA producer: Q pair once, then K/V (or centroid) tiles into a
-//             2-stage ring, finally H (first-order operand) for the correction
-//   warp 1    TMEM owner + single-thread MMA issuer:
-//             S(j) = Q K(j)^T  -> TMEM S[j%2] (128 x 64 FP32)
-//             O   += P(j) V(j) -> TMEM O      (128 x 128 FP32)
-//             C    = Q H       -> TMEM (reuses the S columns after the loop)
-//   warps 2-5 softmax: thread r owns query row r (TMEM lane r); reads S with
-//             tcgen05.ld, masks/scales in the log2 domain, online max with
-//             lazy O rescaling (only when the max grows by > 2^8), writes P as
-//             BF16 into a 128-byte-swizzled shared tile, and finally reads O
-//             and C to produce (O + tail_mass * corr_scale * C) / l.
-// TMEM: 256 columns (O 0-127, S0 128-191, S1 192-255) so two CTAs share an SM.
+//             5-stage ring, finally H (first-order operand) for the correction
+//   warp 1    TMEM owner (512 columns) + single-thread MMA issuer:
+//             S(j) = Q K(j)^T  -> TMEM S of warpgroup j%2 (128 x 64 FP32)
+//             O   += P(j) V(j) -> TMEM O of warpgroup j%2 (128 x 128 FP32)
+//             C    = Q H       -> TMEM (reuses warpgroup 0's S columns)
+//   warps 2-5 / 6-9  two softmax warpgroups taking alternate key tiles (split
+//             K inside the CTA): thread r owns query row r (TMEM lane r);
+//             reads S with tcgen05.ld, computes exp2 of the scaled logits
+//             with packed f32x2 arithmetic, keeps a lazy running max (O is
+//             rescaled in TMEM only when the max grows by more than 2^8), and
+//             writes P as 16-bit into its own 128-byte-swizzled shared tile.
+//             At the end the two partial softmaxes are merged and
+//             (O + tail_mass * corr_scale * C) / l is stored, each warpgroup
+//             writing half of the columns.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -39,20 +42,24 @@ namespace {
 
 using namespace umma;
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;  // K producer, MMA, 2 softmax warpgroups, V producer
+constexpr int kStages = 5;
 constexpr int kMaxList = 192;  // union of two selected lists
 constexpr int kMaxSelWords = 32;
 constexpr uint32_t kQBytes = 128 * 128 * 2;
-constexpr uint32_t kStageBytes = 2 * 64 * 128 * 2;  // K + V tile
+constexpr uint32_t kPBytes = 128 * 64 * 2;
+constexpr uint32_t kSlotBytes = 64 * 128 * 2;  // one K or V tile (two 8 KB d-halves)
 
 struct __align__(8) Misc {
   uint64_t q_full;
-  uint64_t kv_full[2];
-  uint64_t kv_empty[2];
-  uint64_t s_full[2];
-  uint64_t s_free[2];
-  uint64_t p_full;
-  uint64_t pv_done;
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
+  uint64_t s_full[2][2];
+  uint64_t s_free[2][2];
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
   uint64_t c_full;
   uint64_t mma_done;
   uint32_t tmem;
@@ -64,19 +71,19 @@ struct __align__(8) Misc {
 };
 
 struct SmemLayout {
-  static constexpr uint32_t q = 0;                     // [2 d-halves][128 rows][128 B]
-  static constexpr uint32_t kv = q + kQBytes;          // [2 stages][K 2x8KB | V 2x8KB]
-  static constexpr uint32_t p = kv + 2 * kStageBytes;  // [128 rows][128 B]
-  static constexpr uint32_t misc = p + 128 * 128;
+  static constexpr uint32_t q = 0;                 // [2 d-halves][128 rows][128 B]
+  static constexpr uint32_t p = q + kQBytes;       // [2 warpgroups][128 rows][128 B]
+  static constexpr uint32_t k = p + 2 * kPBytes;   // [stages][2 d-halves x 8 KB]
+  static constexpr uint32_t v = k + kStages * kSlotBytes;
+  static constexpr uint32_t misc = v + kStages * kSlotBytes;
   static constexpr uint32_t total = misc + sizeof(Misc);
 };
+static_assert(SmemLayout::total <= 232448, "shared memory budget");
 
-// Tile descriptor: kind (0 = centroid tail, 1 = key block), block index and
-// the two-bit mask of query halves it applies to.
 struct Tile {
-  int tail;
+  int tail;  // 1: centroid tail tile, 0: key block
   int blk;
-  uint32_t mask;
+  uint32_t mask;  // bit h: applies to query half h
 };
 
 __device__ __forceinline__ Tile tile_at(const UmmaArgs& a, const Misc& m, int j, int ntail) {
@@ -116,17 +123,95 @@ __device__ __forceinline__ void load_block(const CUtensorMap* map, const UmmaArg
   }
 }
 
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// (lo, hi) = (x0, x1) * (s, s) + (t, t) with one packed f32x2 FMA
+__device__ __forceinline__ void fma2(float& lo, float& hi, float x0, float x1, float s, float t) {
+  uint64_t x, sv, tv, d;
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(x) : "f"(x0), "f"(x1));
+  asm("mov.b64 %0, {%1, %1};\n" : "=l"(sv) : "f"(s));
+  asm("mov.b64 %0, {%1, %1};\n" : "=l"(tv) : "f"(t));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(d) : "l"(x), "l"(sv), "l"(tv));
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(lo), "=f"(hi) : "l"(d));
+}
+
+// (a0, a1) += (b0, b1) with one packed f32x2 add
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+  uint64_t x, y, d;
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(x) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(y) : "f"(b0), "f"(b1));
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(a0), "=f"(a1) : "l"(d));
+}
+
+// S(j) = Q K(j)^T into the S buffer of warpgroup j%2; frees K slot on completion.
 template <bool BF16>
-__global__ void __launch_bounds__(kThreads, 2)
+__device__ __forceinline__ bool issue_s(Misc& m, char* k_s, uint32_t q_addr, uint32_t tmem, const UmmaArgs& a,
+                                        volatile int* abort_flag, int j, long long* trace) {
+  const int s = j % kStages;
+  const int w = j & 1;
+  const int i = j >> 1;
+  const int sb = i & 1;
+  if (!mbar_wait(&m.k_full[s], (j / kStages) & 1, abort_flag, a.status, 4)) return false;
+  if (!mbar_wait(&m.s_free[w][sb], ((i >> 1) & 1) ^ 1, abort_flag, a.status, 5)) return false;
+  tc_fence_after();
+  if (trace && j < 256) trace[6 * j + 1] = clock64();
+  const uint32_t idesc_s = idesc_f16(128, 64, BF16, false, false);
+  const uint32_t k_addr = smem_u32(k_s + s * kSlotBytes);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+    const uint64_t db = smem_desc_sw128(k_addr + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+    mma_ss(tmem + w * 256 + 128 + 64 * sb, da, db, idesc_s, kk > 0 ? 1u : 0u);
+  }
+  mma_commit(&m.s_full[w][sb]);
+  mma_commit(&m.k_empty[s]);
+  return true;
+}
+
+// O(w) += P(w) V(jj): the P.V product of key tile jj (warpgroup w = jj % 2).
+template <bool BF16>
+__device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, const UmmaArgs& a,
+                                         volatile int* abort_flag, int jj) {
+  const int w = jj & 1;
+  const int i = jj >> 1;
+  if (!mbar_wait(&m.p_full[w], i & 1, abort_flag, a.status, 2)) return false;
+  if (!mbar_wait(&m.v_full[jj % kStages], (jj / kStages) & 1, abort_flag, a.status, 12)) return false;
+  tc_fence_after();
+  const uint32_t idesc_o = idesc_f16(128, 128, BF16, false, true);
+  const uint32_t p_addr = smem_u32(smem + SmemLayout::p + w * kPBytes);
+  const uint32_t v_addr = smem_u32(smem + SmemLayout::v + (jj % kStages) * kSlotBytes);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const uint64_t da = smem_desc_sw128(p_addr + kk * 32, 16, 1024);
+    const uint64_t db = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
+    mma_ss(tmem + w * 256, da, db, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+  }
+  mma_commit(&m.pv_done[w]);
+  mma_commit(&m.v_empty[jj % kStages]);
+  return true;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
 attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                  const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap kc_map,
                  const __grid_constant__ CUtensorMap vc_map, const __grid_constant__ CUtensorMap h_map,
-                 const UmmaArgs a) {
+                 const __grid_constant__ UmmaArgs a) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ __align__(1024) char smem[];
   Misc& m = *reinterpret_cast<Misc*>(smem + SmemLayout::misc);
   char* q_s = smem + SmemLayout::q;
-  char* kv_s = smem + SmemLayout::kv;
-  char* p_s = smem + SmemLayout::p;
+  char* k_s = smem + SmemLayout::k;
+  char* v_s = smem + SmemLayout::v;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int pair = blockIdx.x;
@@ -145,17 +230,22 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       m.abort_flag = 0;
     }
     mbar_init(&m.q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&m.kv_full[s], 1);
-      mbar_init(&m.kv_empty[s], 1);
-      mbar_init(&m.s_full[s], 1);
-      mbar_init(&m.s_free[s], 4);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&m.k_full[s], 1);
+      mbar_init(&m.k_empty[s], 1);
+      mbar_init(&m.v_full[s], 1);
+      mbar_init(&m.v_empty[s], 1);
     }
-    mbar_init(&m.p_full, 4);
-    mbar_init(&m.pv_done, 1);
+    for (int w = 0; w < 2; ++w) {
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&m.s_full[w][b], 1);
+        mbar_init(&m.s_free[w][b], 4);
+      }
+      mbar_init(&m.p_full[w], 4);
+      mbar_init(&m.pv_done[w], 1);
+    }
     mbar_init(&m.c_full, 1);
     mbar_init(&m.mma_done, 1);
-    // key tile list
     int nlist = 0;
     if (a.mode == 1) {
       const int32_t* la = a.indices + (int64_t(bh) * a.nqb + qa) * a.nsel;
@@ -198,102 +288,96 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       m.sel[half][w] = a.sel_bits[(int64_t(bh) * a.nqb + qblk) * words + w];
     }
   }
-  if (warp == 1) tmem_alloc<256>(&m.tmem);
+  if (warp == 1) tmem_alloc<512>(&m.tmem);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = m.tmem;
   const int n = m.ntiles;
   volatile int* abort_flag = &m.abort_flag;
+  long long* trace = (a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0) ? a.trace : nullptr;
+  if (trace && threadIdx.x == 0) trace[6 * 256] = clock64();
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ Q / K / H producer
     if (lane == 0 && !*abort_flag) {
       tma_prefetch_desc(&q_map);
       tma_prefetch_desc(&k_map);
-      tma_prefetch_desc(&v_map);
       mbar_expect_tx(&m.q_full, kQBytes);
       for (int half = 0; half < 2; ++half)
         for (int dh = 0; dh < 2; ++dh)
           load_block(&q_map, a, q_s + dh * 16384 + half * 8192, &m.q_full, a.q_kind, bh, half ? qb : qa, dh);
-      const int total = n + (a.has_corr ? 1 : 0);
+      // key tiles 0..n-1, then the two 64-column halves of H as "tiles" n, n+1
+      const int total = n + (a.has_corr ? 2 : 0);
       for (int j = 0; j < total; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&m.kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, a.status, 1)) break;
-        char* stage = kv_s + s * kStageBytes;
-        mbar_expect_tx(&m.kv_full[s], kStageBytes);
+        const int s = j % kStages;
+        if (!mbar_wait(&m.k_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, a.status, 1)) break;
+        char* slot = k_s + s * kSlotBytes;
+        if (trace && j < 256) trace[6 * j] = clock64();
         if (j < n) {
+          mbar_expect_tx(&m.k_full[s], kSlotBytes);
           const Tile t = tile_at(a, m, j, ntail);
           for (int dh = 0; dh < 2; ++dh) {
-            if (t.tail) {
-              tma_load_3d(stage + dh * 8192, &kc_map, &m.kv_full[s], dh * 64, t.blk * 64, bh);
-              tma_load_3d(stage + 16384 + dh * 8192, &vc_map, &m.kv_full[s], dh * 64, t.blk * 64, bh);
-            } else {
-              load_block(&k_map, a, stage + dh * 8192, &m.kv_full[s], a.kv_kind, bh, t.blk, dh);
-              load_block(&v_map, a, stage + 16384 + dh * 8192, &m.kv_full[s], a.kv_kind, bh, t.blk, dh);
-            }
+            if (t.tail) tma_load_3d(slot + dh * 8192, &kc_map, &m.k_full[s], dh * 64, t.blk * 64, bh);
+            else load_block(&k_map, a, slot + dh * 8192, &m.k_full[s], a.kv_kind, bh, t.blk, dh);
           }
         } else {
-          for (int dh = 0; dh < 2; ++dh) tma_load_3d(stage + dh * 16384, &h_map, &m.kv_full[s], dh * 64, 0, bh);
+          // H[:, 64*(j-n) : 64*(j-n)+64]: 128 rows x 128 B
+          mbar_expect_tx(&m.k_full[s], kSlotBytes);
+          tma_load_3d(slot, &h_map, &m.k_full[s], (j - n) * 64, 0, bh);
+        }
+      }
+    }
+  } else if (warp == 10) {
+    // ------------------------------------------------------------ V producer
+    if (lane == 0 && !*abort_flag) {
+      tma_prefetch_desc(&v_map);
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kStages;
+        if (!mbar_wait(&m.v_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, a.status, 13)) break;
+        char* slot = v_s + s * kSlotBytes;
+        mbar_expect_tx(&m.v_full[s], kSlotBytes);
+        const Tile t = tile_at(a, m, j, ntail);
+        for (int dh = 0; dh < 2; ++dh) {
+          if (t.tail) tma_load_3d(slot + dh * 8192, &vc_map, &m.v_full[s], dh * 64, t.blk * 64, bh);
+          else load_block(&v_map, a, slot + dh * 8192, &m.v_full[s], a.kv_kind, bh, t.blk, dh);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      const uint32_t idesc_s = idesc_f16(128, 64, BF16, false, false);
-      const uint32_t idesc_o = idesc_f16(128, 128, BF16, false, true);
       const uint32_t q_addr = smem_u32(q_s);
-      const uint32_t p_addr = smem_u32(p_s);
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(&m.p_full, i & 1, abort_flag, a.status, 2)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(kv_s + (i & 1) * kStageBytes + 16384);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t da = smem_desc_sw128(p_addr + kk * 32, 16, 1024);
-          const uint64_t db = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
-          mma_ss(tmem, da, db, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(&m.pv_done);
-        mma_commit(&m.kv_empty[i & 1]);
-        return true;
-      };
+      // Order: S(0..3), then for each tile j: P.V(j) followed by S(j+4).  Each
+      // warpgroup has two S buffers, so S(j+2) is ready before it finishes
+      // the softmax of tile j; K slots are released as soon as S completes.
       bool ok = mbar_wait(&m.q_full, 0, abort_flag, a.status, 3);
+      int issued = 0;
+      while (ok && issued < n && issued < 4) ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, issued++, trace);
       for (int j = 0; ok && j < n; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&m.kv_full[s], (j >> 1) & 1, abort_flag, a.status, 4)) break;
-        if (!mbar_wait(&m.s_free[s], ((j >> 1) & 1) ^ 1, abort_flag, a.status, 5)) break;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(kv_s + s * kStageBytes);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          const uint64_t db = smem_desc_sw128(k_addr + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-          mma_ss(tmem + 128 + 64 * s, da, db, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(&m.s_full[s]);
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
-        }
+        ok = issue_pv<BF16>(m, smem, tmem, a, abort_flag, j);
+        if (ok && issued < n) ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, issued++, trace);
       }
-      if (ok && n > 0) ok = issue_pv(n - 1);
       if (ok && a.has_corr) {
-        const int s = n & 1;
-        if (mbar_wait(&m.kv_full[s], (n >> 1) & 1, abort_flag, a.status, 6)) {
+        // C = Q H as two N=64 products, one per 64-column half of H
+        const uint32_t idesc_c = idesc_f16(128, 64, BF16, false, true);
+        for (int hh = 0; ok && hh < 2; ++hh) {
+          const int j = n + hh;
+          const int s = j % kStages;
+          ok = mbar_wait(&m.k_full[s], (j / kStages) & 1, abort_flag, a.status, 6);
+          if (!ok) break;
           tc_fence_after();
-          const uint32_t h_addr = smem_u32(kv_s + s * kStageBytes);
+          const uint32_t h_addr = smem_u32(k_s + s * kSlotBytes);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t da = smem_desc_sw128(q_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
             const uint64_t db = smem_desc_sw128(h_addr + kk * 2048, 16384, 1024);
-            mma_ss(tmem + 128, da, db, idesc_o, kk > 0 ? 1u : 0u);
+            mma_ss(tmem + 128 + 64 * hh, da, db, idesc_c, kk > 0 ? 1u : 0u);
           }
-          mma_commit(&m.c_full);
         }
+        if (ok) mma_commit(&m.c_full);
       }
-      // every MMA this thread issued has completed before TMEM is released
+      // every MMA this thread issued completes before TMEM is released
       // (bounded by time only, even after an abort)
       mma_commit(&m.mma_done);
       int no_abort = 0;
@@ -301,53 +385,90 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     }
   } else {
     // ------------------------------------------------------------ softmax
+    const int wg = (warp - 2) >> 2;   // 0 or 1
     const int sub = warp & 3;         // TMEM sub-partition of this warp
     const int row = sub * 32 + lane;  // query row within the pair
     const int half = row >> 6;        // 0: block qa, 1: block qb
     const int qblk = half ? qb : qa;
     const uint32_t lane_base = static_cast<uint32_t>(sub * 32) << 16;
+    const uint32_t o_base = tmem + lane_base + wg * 256;
     const int tq_row = qblk * 64 + (row & 63);
     float mrun = -INFINITY, lrun = 0.f, tmass = 0.f;
-    char* prow = p_s + (row >> 3) * 1024 + (row & 7) * 128;
-    for (int j = 0; j < n; ++j) {
-      const int s = j & 1;
+    const int nb_ = a.nb, causal_ = a.causal, tk_ = a.tk;
+    const float log2_last_ = a.log2_last, scale_log2_ = a.scale_log2;
+    char* prow = smem + SmemLayout::p + wg * kPBytes + (row >> 3) * 1024 + (row & 7) * 128;
+    int i = 0;
+    bool ok = true;
+    for (int j = wg; j < n; j += 2, ++i) {
+      const int sb = i & 1;
       const Tile t = tile_at(a, m, j, ntail);
       const bool active = ((t.mask >> half) & 1u) != 0;
-      uint32_t v[64];
-      if (!mbar_wait(&m.s_full[s], (j >> 1) & 1, abort_flag, a.status, 8)) break;
+      if (!mbar_wait(&m.s_full[wg][sb], (i >> 1) & 1, abort_flag, a.status, 8)) {
+        ok = false;
+        break;
+      }
+      if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 3] = clock64();
       tc_fence_after();
-      tmem_ld32(tmem + lane_base + 128 + 64 * s, v);
-      tmem_ld32(tmem + lane_base + 128 + 64 * s + 32, v + 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&m.s_free[s]);
+      const uint32_t s_addr = o_base + 128 + 64 * sb;
+      // logits in the log2 domain: x = s * scale_log2 (+ log2 len for the tail),
+      // masked -> -inf.  Two passes over the S columns (32 at a time) keep the
+      // register footprint small: max first, then exp2 + P.
+      const int klen = t.tail ? 64 : min(64, tk_ - t.blk * 64);
+      const bool plain = !t.tail && klen == 64 && !causal_;
+      // masked columns of this tile as two 32-bit words (bit c = column c),
+      // and the column that carries the last (ragged) block's log2 length
+      uint32_t bad0 = 0u, bad1 = 0u;
+      int lastc = -1;
+      float bias = 0.f;
+      if (!plain) {
+        uint64_t bad;
+        if (t.tail) {
+          const int c0 = t.blk * 64;
+          const uint32_t w0 = m.sel[half][c0 >> 5];
+          const uint32_t w1 = (c0 + 32) < nb_ ? m.sel[half][(c0 >> 5) + 1] : 0u;
+          const int valid = min(64, nb_ - c0);
+          bad = (static_cast<uint64_t>(w1) << 32) | w0;
+          if (valid < 64) bad |= ~0ull << valid;
+          lastc = nb_ - 1 - c0;
+          bias = 6.0f;  // log2(64)
+        } else {
+          bad = klen < 64 ? (~0ull << klen) : 0ull;
+          if (causal_) {
+            const int lim = tq_row - t.blk * 64;  // columns > lim are masked
+            if (lim < 63) bad |= lim < 0 ? ~0ull : (~0ull << (lim + 1));
+          }
+        }
+        bad0 = static_cast<uint32_t>(bad);
+        bad1 = static_cast<uint32_t>(bad >> 32);
+      }
+      const float last_bias = log2_last_;
       float alpha = 1.f;
       bool rescale = false;
       if (active) {
         float mx = -INFINITY;
-        if (t.tail) {
-          const uint32_t w0 = m.sel[half][(t.blk * 64) >> 5];
-          const uint32_t w1 = (t.blk * 64 + 32) < a.nb ? m.sel[half][((t.blk * 64) >> 5) + 1] : 0u;
+#pragma unroll 1
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t v[32];
+          tmem_ld32(s_addr + 32 * h2, v);
+          tmem_wait_ld();
+          if (h2 == 0 && trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 2] = clock64();
+          if (plain) {
+            float m0 = fmaxf(__uint_as_float(v[0]), __uint_as_float(v[1]));
+            float m1 = fmaxf(__uint_as_float(v[2]), __uint_as_float(v[3]));
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const int jj = t.blk * 64 + c;
-            const uint32_t bit = c < 32 ? (w0 >> c) & 1u : (w1 >> (c - 32)) & 1u;
-            const bool masked = jj >= a.nb || bit;
-            const float bias = jj == a.nb - 1 ? a.log2_last : 6.0f;  // log2(64) = 6
-            const float xv = masked ? -INFINITY : fmaf(__uint_as_float(v[c]), a.scale_log2, bias);
-            v[c] = __float_as_uint(xv);
-            mx = fmaxf(mx, xv);
-          }
-        } else {
-          const int klen = min(64, a.tk - t.blk * 64);
+            for (int c = 4; c < 32; c += 4) {
+              m0 = max3(m0, __uint_as_float(v[c]), __uint_as_float(v[c + 1]));
+              m1 = max3(m1, __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
+            }
+            mx = fmaxf(mx, fmaxf(m0, m1) * scale_log2_);
+          } else {
+            const uint32_t bw = h2 ? bad1 : bad0;
+            const int lc = lastc - 32 * h2;
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            bool masked = c >= klen;
-            if (a.causal) masked = masked || (t.blk * 64 + c > tq_row);
-            const float xv = masked ? -INFINITY : __uint_as_float(v[c]) * a.scale_log2;
-            v[c] = __float_as_uint(xv);
-            mx = fmaxf(mx, xv);
+            for (int c = 0; c < 32; ++c) {
+              const float x = fmaf(__uint_as_float(v[c]), scale_log2_, c == lc ? last_bias : bias);
+              mx = fmaxf(mx, ((bw >> c) & 1u) ? -INFINITY : x);
+            }
           }
         }
         const float mnew = fmaxf(mrun, mx);
@@ -358,82 +479,122 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           mrun = mnew;
           rescale = true;
         }
-        float sum = 0.f;
-        if (mrun == -INFINITY) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) v[c] = 0u;
-        } else {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const float pv = ex2(__uint_as_float(v[c]) - mrun);
-            v[c] = __float_as_uint(pv);
-            sum += pv;
-          }
-        }
-        lrun = lrun * alpha + sum;
-        tmass = tmass * alpha + (t.tail ? sum : 0.f);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) v[c] = 0u;
       }
-      if (j >= 1 && !mbar_wait(&m.pv_done, (j - 1) & 1, abort_flag, a.status, 9)) break;
+      if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 4] = clock64();
+      // the P tile and O of this warpgroup are free once its previous P.V is done
+      if (i >= 1 && !mbar_wait(&m.pv_done[wg], (i - 1) & 1, abort_flag, a.status, 9)) {
+        ok = false;
+        break;
+      }
       if (__any_sync(0xffffffffu, rescale)) {
         tc_fence_after();
 #pragma unroll 1
         for (int c0 = 0; c0 < 128; c0 += 32) {
           uint32_t o[32];
-          tmem_ld32(tmem + lane_base + c0, o);
+          tmem_ld32(o_base + c0, o);
           tmem_wait_ld();
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tmem_st32(tmem + lane_base + c0, o);
+          tmem_st32(o_base + c0, o);
         }
         tmem_wait_st();
       }
-      // P row -> 128-byte swizzled K-major tile (chunk c of row r at c ^ (r % 8))
+      // P = exp2(x - m) -> 16-bit, straight into the 128-byte swizzled K-major
+      // tile (16-byte chunk c of row r lives at chunk c ^ (r % 8))
+      if (active && mrun != -INFINITY) {
+        const float neg = -mrun;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll 1
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t v[32];
+          tmem_ld32(s_addr + 32 * h2, v);
+          tmem_wait_ld();
+          float mul = scale_log2_;
+          if (!plain) {
+            const uint32_t bw = h2 ? bad1 : bad0;
+            const int lc = lastc - 32 * h2;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 w;
-        w.x = Cvt<typename std::conditional<BF16, __nv_bfloat16, __half>::type>::pack2(__uint_as_float(v[8 * c]),
-                                                                                      __uint_as_float(v[8 * c + 1]));
-        w.y = Cvt<typename std::conditional<BF16, __nv_bfloat16, __half>::type>::pack2(__uint_as_float(v[8 * c + 2]),
-                                                                                      __uint_as_float(v[8 * c + 3]));
-        w.z = Cvt<typename std::conditional<BF16, __nv_bfloat16, __half>::type>::pack2(__uint_as_float(v[8 * c + 4]),
-                                                                                      __uint_as_float(v[8 * c + 5]));
-        w.w = Cvt<typename std::conditional<BF16, __nv_bfloat16, __half>::type>::pack2(__uint_as_float(v[8 * c + 6]),
-                                                                                      __uint_as_float(v[8 * c + 7]));
-        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = w;
+            for (int c = 0; c < 32; ++c) {
+              const float x = fmaf(__uint_as_float(v[c]), scale_log2_, c == lc ? last_bias : bias);
+              v[c] = __float_as_uint(((bw >> c) & 1u) ? -INFINITY : x);
+            }
+            mul = 1.f;
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float x0, x1;
+              fma2(x0, x1, __uint_as_float(v[8 * c + 2 * e]), __uint_as_float(v[8 * c + 2 * e + 1]), mul, neg);
+              const float p0 = ex2(x0);
+              const float p1 = ex2(x1);
+              add2(s0, s1, p0, p1);
+              w4[e] = Cvt<T>::pack2(p0, p1);
+            }
+            const int chunk = 4 * h2 + c;
+            *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+        }
+        const float sum = s0 + s1;
+        lrun = lrun * alpha + sum;
+        tmass = tmass * alpha + (t.tail ? sum : 0.f);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(prow + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&m.s_free[wg][sb]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&m.p_full);
+      if (lane == 0) mbar_arrive(&m.p_full[wg]);
+      if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 5] = clock64();
     }
-    // ---- epilogue
-    bool ok = n == 0 || mbar_wait(&m.pv_done, (n - 1) & 1, abort_flag, a.status, 10);
+    // ---- merge the two partial softmaxes, add the correction, store
+    if (ok && i >= 1) ok = mbar_wait(&m.pv_done[wg], (i - 1) & 1, abort_flag, a.status, 10);
+    // partial statistics [m | l | tail mass] x 128 rows per warpgroup go into
+    // the V ring (every P.V has completed once both warpgroups get here)
+    named_barrier_sync(1, 256);
+    float* stat_own = reinterpret_cast<float*>(v_s + wg * 2048);
+    const float* stat0 = reinterpret_cast<const float*>(v_s);
+    const float* stat1 = reinterpret_cast<const float*>(v_s + 2048);
+    stat_own[row] = mrun;
+    stat_own[128 + row] = lrun;
+    stat_own[256 + row] = tmass;
+    named_barrier_sync(1, 256);
     if (ok && a.has_corr) ok = mbar_wait(&m.c_full, 0, abort_flag, a.status, 11);
     tc_fence_after();
-    const bool store = ok && (half == 0 || has_b) && tq_row < a.tq;
-    const float inv = lrun > 0.f ? 1.f / lrun : 0.f;
-    const float cw = tmass * a.corr_scale;
+    const float m0 = stat0[row], m1 = stat1[row];
+    const float mm = fmaxf(m0, m1);
+    const float a0 = m0 == -INFINITY ? 0.f : ex2(m0 - mm);
+    const float a1 = m1 == -INFINITY ? 0.f : ex2(m1 - mm);
+    const float lt = stat0[128 + row] * a0 + stat1[128 + row] * a1;
+    const float tt = stat0[256 + row] * a0 + stat1[256 + row] * a1;
+    const bool store = ok && !*abort_flag && (half == 0 || has_b) && tq_row < a.tq;
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    const float cw = tt * a.corr_scale;
     char* orow = store ? a.o.row(bh, tq_row) : nullptr;
+    const uint32_t row_base = tmem + lane_base;
 #pragma unroll 1
-    for (int c0 = 0; c0 < 128; c0 += 32) {
-      uint32_t o[32], cr[32];
-      tmem_ld32(tmem + lane_base + c0, o);
-      if (a.has_corr) tmem_ld32(tmem + lane_base + 128 + c0, cr);
+    for (int c0 = wg * 64; c0 < wg * 64 + 64; c0 += 32) {
+      uint32_t o0[32], o1[32], cr[32];
+      tmem_ld32(row_base + c0, o0);
+      tmem_ld32(row_base + 256 + c0, o1);
+      if (a.has_corr) tmem_ld32(row_base + 128 + c0, cr);
       tmem_wait_ld();
       if (store) {
         uint32_t packed[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          float f0 = __uint_as_float(o[c]);
-          float f1 = __uint_as_float(o[c + 1]);
+          float f0 = __uint_as_float(o0[c]) * a0 + __uint_as_float(o1[c]) * a1;
+          float f1 = __uint_as_float(o0[c + 1]) * a0 + __uint_as_float(o1[c + 1]) * a1;
           if (a.has_corr) {
             f0 = fmaf(__uint_as_float(cr[c]), cw, f0);
             f1 = fmaf(__uint_as_float(cr[c + 1]), cw, f1);
           }
-          packed[c / 2] = Cvt<typename std::conditional<BF16, __nv_bfloat16, __half>::type>::pack2(f0 * inv, f1 * inv);
+          packed[c / 2] = Cvt<T>::pack2(f0 * inv, f1 * inv);
         }
         uint4* dst = reinterpret_cast<uint4*>(orow + c0 * 2);
 #pragma unroll
@@ -441,15 +602,15 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           dst[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
       }
     }
-    if (store && a.lse != nullptr) {
-      a.lse[int64_t(bh) * a.tq + tq_row] = lrun > 0.f ? (mrun + __log2f(lrun)) * 0.6931471805599453f : -INFINITY;
+    if (store && wg == 0 && a.lse != nullptr) {
+      a.lse[int64_t(bh) * a.tq + tq_row] = lt > 0.f ? (mm + __log2f(lt)) * 0.6931471805599453f : -INFINITY;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc<256>(tmem);
+    tmem_dealloc<512>(tmem);
   }
 }
 
@@ -578,6 +739,7 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   a.o = p.o;
   a.lse = p.lse;
   a.status = status;
+  a.trace = p.trace;
   if (p.nb > 0) {
     const int last_len = kv.tokens - 64 * (p.nb - 1);
     a.log2_last = log2f(static_cast<float>(last_len));

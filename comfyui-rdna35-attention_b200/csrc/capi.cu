@@ -16,6 +16,7 @@ namespace {
 
 thread_local char g_error[512] = "";
 thread_local const char* g_last_kernel = "none";
+long long* g_trace = nullptr;  // diagnostics timeline buffer (b2_set_trace)
 
 // B200ATTN_KERNEL=mma forces the warp-level mma.sync attention kernel
 // (kept for layouts the TMA maps cannot express); default: tcgen05 kernel.
@@ -30,10 +31,12 @@ bool umma_enabled() {
 cudaError_t run_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* o, const AttnParams& p,
                           cudaStream_t st) {
   if (umma_enabled() && umma_supported(*q, *k, *v, *o)) {
+    AttnParams pt = p;
+    pt.trace = g_trace;
     bool launched = false;
     int* status = device_status_ptr();
     if (status != nullptr) {
-      const cudaError_t err = launch_attn_umma(*q, *k, *v, *o, p, status, st, &launched);
+      const cudaError_t err = launch_attn_umma(*q, *k, *v, *o, pt, status, st, &launched);
       if (err != cudaSuccess || launched) {
         g_last_kernel = "tcgen05";
         return err;
@@ -171,6 +174,11 @@ extern "C" {
 const char* b2_last_error(void) { return g_error; }
 
 const char* b2_last_kernel(void) { return g_last_kernel; }
+
+int b2_set_trace(long long* device_buffer) {
+  g_trace = device_buffer;
+  return ok();
+}
 
 int b2_read_status(int32_t* status) {
   if (status == nullptr) return fail(B2_ERR_INVALID, "status pointer is NULL");

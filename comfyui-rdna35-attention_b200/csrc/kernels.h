@@ -20,6 +20,7 @@ struct AttnParams {
   float corr_scale;
   float* lse;
   int causal;
+  long long* trace;
 };
 // Arguments of the tcgen05 attention kernel (see attn_umma.cu).
 struct UmmaArgs {
@@ -37,6 +38,7 @@ struct UmmaArgs {
   Rows o;
   float* lse;
   int* status;
+  long long* trace;  // optional clock64 timeline of CTA (0,0): [tile][6] + start
 };
 bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const b2_view& o);
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,

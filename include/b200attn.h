@@ -81,6 +81,10 @@ const char* b2_last_kernel(void);
  * pipeline wait timed out (the kernel then ends early; outputs are invalid).
  * This is the one entry point that synchronises (it copies 4 bytes). */
 int b2_read_status(int32_t* status);
+/* Diagnostics: when device_buffer is not NULL, later tcgen05 attention
+ * launches of this process record clock64() timestamps of CTA (0,0) into it
+ * ([256 tiles][6 events] + start, int64; see attn_umma.cu).  NULL disables. */
+int b2_set_trace(long long* device_buffer);
 int b2_api_version(void);
 /* Writes a NUL-terminated "key=value;..." build description. */
 int b2_build_info(char* buffer, int64_t capacity);
