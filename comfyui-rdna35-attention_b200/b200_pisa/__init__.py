@@ -250,22 +250,30 @@ def forward_spatial_bhtd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exac
 
 
 def generic_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int, scale: float,
-                    first_order: bool = True) -> torch.Tensor:
-    """Generic PISA (generic_pisa.py:141-232 semantics) on contiguous
-    [BH,T,128] fp16/bf16 with T up to 65536: FP32 centroids, routing without
-    the HYD bias, BF16-rounded centred K, optional first-order term."""
-    if q.ndim != 3 or q.shape != k.shape or q.shape != v.shape:
-        raise ValueError("generic PISA requires matching [BH,T,D] q/k/v")
-    if q.shape[2] != HEAD_DIM:
+                    first_order: bool = True, grid: tuple[int, int] | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Generic PISA (generic_pisa.py:141-232 semantics): FP32 centroids,
+    routing without the HYD bias, 16-bit-rounded centred K, optional
+    first-order term.  q/k/v: [BH,T,128] or [B,H,T,128] views (fp16/bf16,
+    head dimension contiguous), T up to 65536.  grid=(h, w) reads the tokens
+    in 8x8-tile order of per-frame h x w rasters (no packing copy); the
+    output (``out`` view or a new tensor shaped like q) is in token order."""
+    if q.ndim not in (3, 4) or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("generic PISA requires matching [BH,T,D] or [B,H,T,D] q/k/v")
+    if q.shape[-1] != HEAD_DIM:
         raise ValueError(f"B200 generic PISA requires D={HEAD_DIM}")
-    blocks = (q.shape[1] + BLOCK_SIZE - 1) // BLOCK_SIZE
+    tokens = q.shape[-2]
+    blocks = (tokens + BLOCK_SIZE - 1) // BLOCK_SIZE
     if blocks > GENERIC_MAX_BLOCKS:
         raise ValueError(f"B200 generic PISA supports at most {GENERIC_MAX_BLOCKS * BLOCK_SIZE} tokens")
     if not (0 <= exact_blocks <= blocks):
         raise ValueError(f"exact_blocks must be in [0,{blocks}].")
-    out = torch.empty_like(q)
-    _native_forward(view(q), view(k), view(v), view(out), q, q.shape[0], q.shape[1], int(exact_blocks),
-                    _float32(scale), -2, _lib.STATS_GENERIC, first_order)
+    if out is None:
+        out = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    order = dict(order=_lib.ORDER_TILED8, grid=tuple(grid)) if grid is not None else {}
+    views = [view(x, **order) for x in (q, k, v, out)]
+    bh = q.shape[0] * (q.shape[1] if q.ndim == 4 else 1)
+    _native_forward(*views, q, bh, tokens, int(exact_blocks), _float32(scale), -2, _lib.STATS_GENERIC, first_order)
     return out
 
 

@@ -1,0 +1,81 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference.
+
+Run in the container that has the reference checkout (read-only):
+    python tests/golden/make_golden.py /path/to/ComfyUI-RDNA35-Attention
+It imports the reference's own Python implementations -- never the product
+package -- and writes tests/golden/golden.pt:
+  * fixed_block: rdna35_block_attention.reference.fixed_block_attention_ref
+    (config 1 shape scaled to 2 heads x 256 tokens; plain and causal);
+  * pisa_hyd: _pisa_reference of native/rdna35_pisa_ck/tests/test_forward.py
+    (the reference's own pure-torch HYD oracle; the native wheel it imports
+    is stubbed because it cannot load without its ROCm build) for T in
+    {65, 128, 256} with exact_blocks 0/1/2 and sink blocks;
+  * pisa_paper: pisa_attention(backend="reference") (paper variant);
+  * h3_pack: pack_minimax_h3_qkv value/identity checks;
+  * tiling: generic_pisa._pack_spatial_blocks / _pack_video_blocks
+    permutations.
+Inputs are regenerated from the seeds stored next to each case.
+"""
+from __future__ import annotations
+
+import importlib.util
+import pathlib
+import sys
+import types
+
+import torch
+
+
+def seeded(shape, seed, dtype=torch.float32):
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn(shape, generator=gen).to(dtype)
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    sys.modules["rdna35_pisa_ck"] = types.ModuleType("rdna35_pisa_ck")  # stub: ROCm-only wheel
+    from rdna35_block_attention.generic_pisa import _pack_spatial_blocks, _pack_video_blocks
+    from rdna35_block_attention.minimax_h3_gfx1151_attention import pack_minimax_h3_qkv
+    from rdna35_block_attention.pisa_attention import pisa_attention
+    from rdna35_block_attention.reference import fixed_block_attention_ref
+
+    spec = importlib.util.spec_from_file_location(
+        "ref_test_forward", pathlib.Path(ref_root) / "native/rdna35_pisa_ck/tests/test_forward.py")
+    test_forward = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(test_forward)
+    pisa_reference = test_forward._pisa_reference
+
+    golden: dict = {"fixed_block": [], "pisa_hyd": [], "pisa_paper": [], "tiling": {}, "h3_pack": {}}
+    for causal in (False, True):
+        q, k, v = (seeded((1, 2, 256, 64), 100 + i) for i in range(3))
+        out = fixed_block_attention_ref(q, k, v, block_size=64, scale=0.125, causal=causal, layout="bhtd")
+        golden["fixed_block"].append({"seeds": (100, 101, 102), "shape": (1, 2, 256, 64), "scale": 0.125,
+                                      "causal": causal, "out": out})
+    for tokens, exact, sink, seed in ((128, 1, None, 19), (65, 1, 0, 23), (65, 1, -1, 23), (256, 2, None, 31),
+                                      (256, 0, None, 37), (128, 2, None, 17)):
+        q, k, v = (seeded((1, tokens, 128), seed * 10 + i, torch.bfloat16) for i in range(3))
+        out = pisa_reference(q, k, v, exact_blocks=exact, sink_block=sink)
+        golden["pisa_hyd"].append({"seeds": tuple(seed * 10 + i for i in range(3)), "tokens": tokens,
+                                   "exact_blocks": exact, "sink_block": sink, "out": out.to(torch.bfloat16)})
+    for tokens, exact, seed in ((256, 2, 41), (200, 1, 43)):
+        q, k, v = (seeded((2, tokens, 128), seed * 10 + i, torch.bfloat16) for i in range(3))
+        out = pisa_attention(q, k, v, exact_blocks=exact, backend="reference")
+        golden["pisa_paper"].append({"seeds": tuple(seed * 10 + i for i in range(3)), "bh": 2, "tokens": tokens,
+                                     "exact_blocks": exact, "out": out})
+    x = torch.arange(256).reshape(1, 1, 256, 1)
+    golden["tiling"]["spatial_16"] = _pack_spatial_blocks(x, 16).flatten()
+    x = torch.arange(9216).reshape(1, 1, 9216, 1)
+    golden["tiling"]["spatial_96"] = _pack_spatial_blocks(x, 96).flatten()
+    x = torch.arange(2 * 32 * 64).reshape(1, 1, 2 * 32 * 64, 1)
+    golden["tiling"]["video_2_32_64"] = _pack_video_blocks(x, (2, 32, 64)).flatten()
+    qkv = torch.arange(1 * 12000 * 3, dtype=torch.float32).reshape(1, 12000, 3, 1, 1)
+    views = [qkv[:, :, i].permute(0, 2, 1, 3) for i in range(3)]
+    pq, pk, pv, profile = pack_minimax_h3_qkv(*views)
+    golden["h3_pack"] = {"profile_12000": profile, "sum": float(pq.sum() + 2 * pk.sum() + 3 * pv.sum())}
+    out_path = pathlib.Path(__file__).resolve().parent / "golden.pt"
+    torch.save(golden, out_path)
+    print(f"wrote {out_path} ({out_path.stat().st_size} bytes)")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

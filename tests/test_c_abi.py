@@ -1,0 +1,61 @@
+"""The in-tree C-ABI library loads without a GPU and exports every entry
+point include/b200attn.h declares; the ctypes table matches the header."""
+import ctypes
+import pathlib
+import re
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "b200attn.h"
+
+
+def declared_functions() -> set[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return set(re.findall(r"\b(b2_[a-z0-9_]+)\s*\(", text))
+
+
+def test_library_exports_every_declared_symbol():
+    from b200_pisa import _lib
+
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    names = declared_functions()
+    assert len(names) >= 15
+    missing = [n for n in sorted(names) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_ctypes_table_covers_the_header():
+    from b200_pisa import _lib
+
+    names = declared_functions()
+    # the allocation-free statistics entry point is bound by its own callers
+    unbound = names - set(_lib.SIGNATURES) - {"b2_pisa_block_stats_noalloc", "b2_noalloc_last_error"}
+    assert not unbound, unbound
+
+
+def test_host_side_calls_without_gpu():
+    from b200_pisa import _lib
+
+    assert _lib.LIB.b2_api_version() == 7
+    assert "architecture=sm_100a" in _lib.build_info_string()
+    assert _lib.LIB.b2_pisa_workspace_bytes(32, 9216, 128, 23) > 0
+    assert _lib.LIB.b2_pisa_workspace_bytes(32, 9216, 64, 23) == -1
+    # no CUDA driver here: the device check fails with a CUDA error, not a crash
+    assert _lib.LIB.b2_check_device(0) in (_lib.B2_ERR_CUDA, _lib.B2_ERR_DEVICE)
+    assert _lib.LIB.b2_last_error()
+
+
+def test_invalid_views_are_rejected_before_any_launch():
+    import torch
+    from b200_pisa import _lib
+
+    x = torch.zeros((1, 2, 64, 128), dtype=torch.bfloat16)
+    good = _lib.view(x)
+    bad = _lib.view(x)
+    bad.stride_t = 3  # not a multiple of 16 bytes
+    rc = _lib.LIB.b2_full_attention(ctypes.byref(good), ctypes.byref(bad), ctypes.byref(good), ctypes.byref(good),
+                                    0.1, None, None)
+    assert rc == _lib.B2_ERR_INVALID and b"strides" in _lib.LIB.b2_last_error()
+    odd = _lib.view(x[..., :120].contiguous())
+    rc = _lib.LIB.b2_pisa_forward(ctypes.byref(odd), ctypes.byref(odd), ctypes.byref(odd), ctypes.byref(odd), 1,
+                                  0.1, -2, 0, 1, None, None)
+    assert rc == _lib.B2_ERR_UNSUPPORTED
