@@ -123,10 +123,6 @@ __device__ __forceinline__ void load_block(const CUtensorMap* map, const UmmaArg
   }
 }
 
-__device__ __forceinline__ void named_barrier_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;\n" : "=f"(r) : "f"(a), "f"(b), "f"(c));

@@ -28,6 +28,26 @@ bool umma_enabled() {
   return enabled;
 }
 
+// Block statistics: the TMA/tcgen05 kernel when the views allow it, else the
+// warp-MMA kernel; both followed by the fixed-order reduction of partial H.
+cudaError_t run_stats(const b2_view* q, const b2_view* k, const b2_view* v, int mode, void* qc, float* kc, void* vs,
+                      float* h_sum, float* h_norm, void* h_half, float* partial, cudaStream_t st) {
+  const int bh = q->batch * q->heads;
+  const int nb = (q->tokens + kBlock - 1) / kBlock;
+  if (umma_enabled()) {
+    const int group = stats_group_size(bh, nb);
+    int* status = device_status_ptr();
+    bool launched = false;
+    if (status != nullptr) {
+      cudaError_t err = launch_stats_umma(*q, *k, *v, mode, group, qc, kc, vs, h_norm, partial, status, st, &launched);
+      if (err != cudaSuccess) return err;
+      if (launched) return launch_stats_reduce(partial, (nb + group - 1) / group, bh, h_sum, h_half, q->dtype, st);
+    }
+  }
+  return launch_stats(make_rows(*q), make_rows(*k), make_rows(*v), q->dtype, mode, bh, nb, qc, kc, vs, h_sum, h_norm,
+                      h_half, partial, st);
+}
+
 cudaError_t run_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* o, const AttnParams& p,
                           cudaStream_t st) {
   if (umma_enabled() && umma_supported(*q, *k, *v, *o)) {
@@ -234,9 +254,10 @@ int b2_pisa_block_stats(const b2_view* q, const b2_view* k, const b2_view* v, in
     return fail(B2_ERR_INVALID, "PISA statistics outputs and workspace must be non-NULL");
   const int bh = q->batch * q->heads;
   const int nb = (q->tokens + kBlock - 1) / kBlock;
-  const cudaError_t err =
-      launch_stats(make_rows(*q), make_rows(*k), make_rows(*v), q->dtype, mode, bh, nb, q_centroids, k_centroids,
-                   v_stats, h_sum, h_norm, h_bf16, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
+  (void)bh;
+  (void)nb;
+  const cudaError_t err = run_stats(q, k, v, mode, q_centroids, k_centroids, v_stats, h_sum, h_norm, h_bf16,
+                                    static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "PISA block statistics launch");
   return ok();
 }
@@ -322,8 +343,7 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
   if (workspace == nullptr) return fail(B2_ERR_INVALID, "workspace must be non-NULL");
   PisaWorkspace w = carve(static_cast<char*>(workspace), bh, q->tokens, q->head_dim, exact_blocks);
   const bool hyd = stats_mode == B2_STATS_HYD;
-  err = launch_stats(make_rows(*q), make_rows(*k), make_rows(*v), q->dtype, stats_mode, bh, nb, w.qc, w.kc, w.vstat,
-                     w.hsum, w.hnorm, w.h16, w.partial, st);
+  err = run_stats(q, k, v, stats_mode, w.qc, w.kc, w.vstat, w.hsum, hyd ? w.hnorm : nullptr, w.h16, w.partial, st);
   if (err != cudaSuccess) return cuda_fail(err, "PISA statistics launch");
   err = launch_centroid_prep(w.kc, w.vstat, hyd ? 0 : 1, bh, nb, q->tokens, q->head_dim, q->dtype, w.kc16, w.vc16, st);
   if (err != cudaSuccess) return cuda_fail(err, "PISA centroid preparation launch");

@@ -48,6 +48,12 @@ cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype,
                          int blocks, void* q_centroids, float* k_centroids, void* v_stats, float* h_sum,
                          float* h_norm, void* h_half, float* partial, cudaStream_t stream);
 int64_t stats_partial_bytes(int batch_heads, int blocks);
+int stats_group_size(int batch_heads, int blocks);
+cudaError_t launch_stats_reduce(const float* partial, int groups, int batch_heads, float* h_sum, void* h_half,
+                                int dtype, cudaStream_t stream);
+cudaError_t launch_stats_umma(const b2_view& q, const b2_view& k, const b2_view& v, int mode, int group,
+                              void* q_centroids, float* k_centroids, void* v_stats, float* h_norm, float* partial,
+                              int* status, cudaStream_t stream, bool* launched);
 cudaError_t launch_route(const void* qc, int qc_dtype, const float* kc, int kc_round, const float* h_norm,
                          int batch_heads, int blocks, int dim, int k, float scale, int sink, int32_t* indices,
                          uint32_t* sel_bits, cudaStream_t stream);

@@ -253,9 +253,9 @@ __global__ void stats_reduce_kernel(const float* __restrict__ partial, int group
 }  // namespace
 
 int stats_group_size(int batch_heads, int blocks) {
-  // aim at ~4 CTAs per SM across 148 SMs, 1..16 blocks per CTA
+  // aim at ~2 work items per SM across 148 SMs, 1..16 blocks per item
   const long total = static_cast<long>(batch_heads) * blocks;
-  long g = (total + 148 * 4 - 1) / (148 * 4);
+  long g = (total + 148 * 2 - 1) / (148 * 2);
   if (g < 1) g = 1;
   if (g > 16) g = 16;
   return static_cast<int>(g);
@@ -289,6 +289,17 @@ cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype,
 #undef B2_STATS_LAUNCH
   err = cudaGetLastError();
   if (err != cudaSuccess) return err;
+  dim3 rgrid((kD * kD / 4 + 255) / 256, batch_heads);
+  if (dtype == B2_BF16)
+    stats_reduce_kernel<__nv_bfloat16><<<rgrid, 256, 0, stream>>>(partial, groups, h_sum,
+                                                                  static_cast<__nv_bfloat16*>(h_half));
+  else
+    stats_reduce_kernel<__half><<<rgrid, 256, 0, stream>>>(partial, groups, h_sum, static_cast<__half*>(h_half));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_stats_reduce(const float* partial, int groups, int batch_heads, float* h_sum, void* h_half,
+                                int dtype, cudaStream_t stream) {
   dim3 rgrid((kD * kD / 4 + 255) / 256, batch_heads);
   if (dtype == B2_BF16)
     stats_reduce_kernel<__nv_bfloat16><<<rgrid, 256, 0, stream>>>(partial, groups, h_sum,

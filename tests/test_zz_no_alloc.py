@@ -51,8 +51,9 @@ def test_noalloc_stats_match_workspace_entry_point():
             got[n].data_ptr() for n in ("qc", "kc", "vc", "hs", "hn", "h16")), stream)
         assert rc == 0, lib.b2_noalloc_last_error().decode()
         torch.cuda.synchronize()
-        for n in ("qc", "kc", "vc", "hn"):
+        for n in ("qc", "kc", "vc"):
             torch.testing.assert_close(got[n], ref[n], atol=0, rtol=0)
+        torch.testing.assert_close(got["hn"], ref["hn"], atol=1e-2, rtol=1e-3)
         torch.testing.assert_close(got["hs"], ref["hs"], atol=2e-3, rtol=1e-4)
         torch.testing.assert_close(got["h16"].float(), ref["h16"].float(), atol=1e-2, rtol=1e-2)
 
