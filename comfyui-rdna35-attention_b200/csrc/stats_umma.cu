@@ -19,7 +19,8 @@
 //              tensor and adds its rows in order), centring of K into the hi/lo
 //              tiles in 16-byte chunks, and (one block later) the norm of the
 //              previous block's H_blk read back from TMEM
-// TMEM (512 columns): H_blk double buffer 0-255, running H 256-383.
+// TMEM (256 columns used): H_blk double buffer; the running H of the item is
+// accumulated in registers from the H_blk read-back.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -43,8 +44,6 @@ struct __align__(8) Misc {
   uint64_t kc_full[2];      // centred K tile written
   uint64_t mma_done[2];     // H_blk[b] ready (and Kc[b] consumed)
   uint64_t hblk_free[2];    // count 8: norm of H_blk[b] read
-  uint64_t acc_done;        // running H of the item complete
-  uint64_t acc_free;        // count 8: running H read back
   uint64_t fin;             // all MMAs of this CTA complete
   uint32_t tmem;
   int abort_flag;
@@ -119,8 +118,6 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
       mbar_init(&m.mma_done[b], 1);
       mbar_init(&m.hblk_free[b], 8);
     }
-    mbar_init(&m.acc_done, 1);
-    mbar_init(&m.acc_free, 8);
     mbar_init(&m.fin, 1);
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -168,8 +165,6 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
         const int g = item - bh * groups;
         const int first = g * a.group;
         const int last = min(a.blocks, first + a.group);
-        // the previous item's running H must have been read back
-        if (it > 0 && !mbar_wait(&m.acc_free, (it - 1) & 1, abort_flag, a.status, 22)) break;
         for (int blk = first; blk < last; ++blk, ++j) {
           const int s = j % kStages;
           const int b = j & 1;
@@ -178,7 +173,7 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
             ok = false;
             break;
           }
-          if (with_norm && !mbar_wait(&m.hblk_free[b], ((j >> 1) & 1) ^ 1, abort_flag, a.status, 25)) {
+          if (!mbar_wait(&m.hblk_free[b], ((j >> 1) & 1) ^ 1, abort_flag, a.status, 25)) {
             ok = false;
             break;
           }
@@ -191,18 +186,12 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
             const uint64_t dv = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
             const uint64_t dh = smem_desc_sw128(hi_addr + kk * 2048, 8192, 1024);
             const uint64_t dl = smem_desc_sw128(lo_addr + kk * 2048, 8192, 1024);
-            const uint32_t acc_first = (blk > first || kk > 0) ? 1u : 0u;
-            mma_ss(tmem + 256, dh, dv, idesc, acc_first);
-            if (with_lo) mma_ss(tmem + 256, dl, dv, idesc, 1u);
-            if (with_norm) {
-              mma_ss(tmem + 128 * b, dh, dv, idesc, kk > 0 ? 1u : 0u);
-              if (with_lo) mma_ss(tmem + 128 * b, dl, dv, idesc, 1u);
-            }
+            mma_ss(tmem + 128 * b, dh, dv, idesc, kk > 0 ? 1u : 0u);
+            if (with_lo) mma_ss(tmem + 128 * b, dl, dv, idesc, 1u);
           }
           mma_commit(&m.mma_done[b]);
           mma_commit(&m.empty[s]);
         }
-        if (ok) mma_commit(&m.acc_done);
       }
       // every MMA issued has completed before TMEM is released (time-bounded)
       mma_commit(&m.fin);
@@ -220,8 +209,12 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
     int j = 0, it = 0;
     int prev_bh = -1, prev_blk = -1;
     bool ok = true;
-    auto finish_norm = [&](int pj, int pbh, int pblk) {
-      // Frobenius norm of H_blk of block pj (TMEM buffer pj & 1)
+    float hacc[64];  // running H: row trow, columns [wg*64, wg*64+64)
+#pragma unroll
+    for (int e = 0; e < 64; ++e) hacc[e] = 0.f;
+    auto finish_block = [&](int pj, int pbh, int pblk) {
+      // read back H_blk of block pj (TMEM buffer pj & 1): add it to the running
+      // H and (HYD) reduce its Frobenius norm
       const int b = pj & 1;
       if (!mbar_wait(&m.mma_done[b], (pj >> 1) & 1, abort_flag, a.status, 26)) {
         ok = false;
@@ -229,25 +222,28 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
       }
       tc_fence_after();
       float s0 = 0.f, s1 = 0.f;
-#pragma unroll 1
-      for (int c0 = wg * 64; c0 < wg * 64 + 64; c0 += 32) {
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + 128 * b + c0, r);
+        tmem_ld32(tmem + lane_base + 128 * b + wg * 64 + 32 * h2, r);
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          s0 = fmaf(__uint_as_float(r[e]), __uint_as_float(r[e]), s0);
-          s1 = fmaf(__uint_as_float(r[e + 1]), __uint_as_float(r[e + 1]), s1);
+          const float x0 = __uint_as_float(r[e]), x1 = __uint_as_float(r[e + 1]);
+          hacc[32 * h2 + e] += x0;
+          hacc[32 * h2 + e + 1] += x1;
+          s0 = fmaf(x0, x0, s0);
+          s1 = fmaf(x1, x1, s1);
         }
       }
       float sq = s0 + s1;
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&m.hblk_free[b]);
+      if (!with_norm) return;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-      if (lane == 0) {
-        m.norm_part[cw] = sq;
-        mbar_arrive(&m.hblk_free[b]);
-      }
+      if (lane == 0) m.norm_part[cw] = sq;
       named_barrier_sync(1, 256);
       if (tid == 0) {
         float total = 0.f;
@@ -270,19 +266,28 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
         }
         const char* st = smem + Layout::stages + s * kStageBytes;
         // Kc buffer b was last read by the MMAs of block j-2
-        if (j >= 2 && !with_norm && !mbar_wait(&m.mma_done[b], ((j - 2) >> 1) & 1, abort_flag, a.status, 28)) {
-          ok = false;
-          break;
-        }
         // ---- column sums, rows in order (threads 0..191: tensor x column pair)
         if (tid < 192) {
           const int tensor = tid >> 6;
           const int col = (tid & 63) * 2;
           const char* tile = st + tensor * kTile;
           float s0 = 0.f, s1 = 0.f;
-#pragma unroll 4
-          for (int r = 0; r < len; ++r) {
-            const uint32_t w = *reinterpret_cast<const uint32_t*>(tile + sw_off(r, col));
+          // offset of (row 8*rr + u, col) = base + rr*1024 + u*128 + ((chunk ^ u) << 4)
+          const char* base = tile + (col >> 6) * 8192 + ((col & 7) << 1);
+          const int chunk = (col & 63) >> 3;
+          const int full_rows = len & ~7;
+#pragma unroll 1
+          for (int rr = 0; rr < full_rows; rr += 8) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const uint32_t w = *reinterpret_cast<const uint32_t*>(base + (rr + u) * 128 + ((chunk ^ u) << 4));
+              const T* pr = reinterpret_cast<const T*>(&w);
+              s0 += Cvt<T>::to_f(pr[0]);
+              s1 += Cvt<T>::to_f(pr[1]);
+            }
+          }
+          for (int r = full_rows; r < len; ++r) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(base + r * 128 + ((chunk ^ (r & 7)) << 4));
             const T* pr = reinterpret_cast<const T*>(&w);
             s0 += Cvt<T>::to_f(pr[0]);
             s1 += Cvt<T>::to_f(pr[1]);
@@ -350,35 +355,23 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
           mbar_arrive(&m.kc_full[b]);
           mbar_arrive(&m.empty[s]);
         }
-        if (with_norm && prev_blk >= 0) finish_norm(j - 1, prev_bh, prev_blk);
+        if (prev_blk >= 0) finish_block(j - 1, prev_bh, prev_blk);
         prev_bh = bh;
         prev_blk = blk;
       }
       if (!ok) break;
-      if (with_norm && prev_blk >= 0) {
-        finish_norm(j - 1, prev_bh, prev_blk);
+      if (prev_blk >= 0) {
+        finish_block(j - 1, prev_bh, prev_blk);
         prev_blk = -1;
       }
       // running H of this item -> partial[bh][g] (each warpgroup half the columns)
-      if (!mbar_wait(&m.acc_done, it & 1, abort_flag, a.status, 29)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float* dst = a.partial + (int64_t(bh) * groups + g) * 128 * 128 + int64_t(trow) * 128;
-#pragma unroll 1
-      for (int c0 = wg * 64; c0 < wg * 64 + 64; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + 256 + c0, r);
-        tmem_wait_ld();
+      if (!ok) break;
+      float* dst = a.partial + (int64_t(bh) * groups + g) * 128 * 128 + int64_t(trow) * 128 + wg * 64;
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(dst + c0 + e) = make_float4(__uint_as_float(r[e]), __uint_as_float(r[e + 1]),
-                                                                 __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+      for (int e = 0; e < 64; e += 4) {
+        *reinterpret_cast<float4*>(dst + e) = make_float4(hacc[e], hacc[e + 1], hacc[e + 2], hacc[e + 3]);
+        hacc[e] = hacc[e + 1] = hacc[e + 2] = hacc[e + 3] = 0.f;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&m.acc_free);
     }
   }
   tc_fence_before();
