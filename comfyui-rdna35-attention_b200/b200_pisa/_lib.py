@@ -66,7 +66,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2_stats_workspace_bytes": (_I64, [_I32, _I32, _I32]),
     "b2_pisa_block_stats": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
     "b2_pisa_route": (ctypes.c_int, [_VP, _I32, _VP, _I32, _VP, _I32, _I32, _I32, _I32, _F32, _I32, _VP, _VP, _VP]),
-    "b2_pisa_attention": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _VP, _I32, _VP, _VP, _VP, _VP, _F32, _VP, _VP]),
+    "b2_pisa_attention": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _F32, _VP, _VP]),
+    "b2_pisa_pair": (ctypes.c_int, [_VP, _I32, _I32, _VP, _VP]),
     "b2_pisa_workspace_bytes": (_I64, [_I32, _I32, _I32, _I32]),
     "b2_pisa_forward": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _I32, _F32, _I32, _I32, _I32, _VP, _VP]),
     "b2_full_attention": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _F32, _VP, _VP]),

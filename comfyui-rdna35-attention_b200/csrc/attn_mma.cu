@@ -377,7 +377,7 @@ cudaError_t launch_attn_mma(const AttnParams& p, int dtype, int batch_heads, cud
 #define B2_ATTN_LAUNCH(T, DD)                                                                              \
   do {                                                                                                     \
     auto kern = attn_kernel<T, DD>;                                                                        \
-    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
+    err = ensure_smem(reinterpret_cast<const void*>(kern), static_cast<int>(smem)); \
     if (err != cudaSuccess) return err;                                                                    \
     kern<<<grid, kThreads, smem, stream>>>(p);                                                             \
   } while (0)

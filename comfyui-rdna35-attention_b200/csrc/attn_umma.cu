@@ -212,8 +212,13 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
   const int lane = threadIdx.x & 31;
   const int pair = blockIdx.x;
   const int bh = blockIdx.y;
-  const int qa = 2 * pair;
-  const int qb = 2 * pair + 1;
+  int qa = 2 * pair;
+  int qb = 2 * pair + 1;
+  if (a.pairs != nullptr) {
+    qa = a.pairs[(int64_t(bh) * gridDim.x + pair) * 2];
+    qb = a.pairs[(int64_t(bh) * gridDim.x + pair) * 2 + 1];
+    if (qb < 0) qb = a.nqb;  // single block: half B inactive
+  }
   const bool has_b = qb < a.nqb;
   const int ntail = a.nb > 0 ? (a.nb + 63) / 64 : 0;
   const int words = (a.nb + 31) >> 5;
@@ -736,6 +741,7 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   a.lse = p.lse;
   a.status = status;
   a.trace = p.trace;
+  a.pairs = p.mode == 1 ? p.pairs : nullptr;
   if (p.nb > 0) {
     const int last_len = kv.tokens - 64 * (p.nb - 1);
     a.log2_last = log2f(static_cast<float>(last_len));
@@ -754,11 +760,11 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   dim3 grid((a.nqb + 1) / 2, bh);
   cudaError_t err;
   if (qv.dtype == B2_BF16) {
-    err = cudaFuncSetAttribute(attn_umma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<true>), int(smem));
     if (err != cudaSuccess) return err;
     attn_umma_kernel<true><<<grid, kThreads, smem, stream>>>(q_map, k_map, v_map, kc_map, vc_map, h_map, a);
   } else {
-    err = cudaFuncSetAttribute(attn_umma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<false>), int(smem));
     if (err != cudaSuccess) return err;
     attn_umma_kernel<false><<<grid, kThreads, smem, stream>>>(q_map, k_map, v_map, kc_map, vc_map, h_map, a);
   }

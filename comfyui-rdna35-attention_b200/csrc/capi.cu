@@ -5,10 +5,30 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 #include <cstring>
 
 #include "kernels.h"
 
+
+namespace b2 {
+cudaError_t ensure_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(kernel, dev);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess) done[key] = bytes;
+  return err;
+}
+}  // namespace b2
 
 using namespace b2;
 
@@ -129,6 +149,7 @@ struct PisaWorkspace {
   void* vc16;
   int32_t* indices;
   uint32_t* sel;
+  int32_t* pairs;
   float* partial;
   size_t total;
 };
@@ -154,6 +175,7 @@ PisaWorkspace carve(char* base, int bh, int tokens, int dim, int k) {
   w.vc16 = take(cent * 2);
   w.indices = reinterpret_cast<int32_t*>(take(size_t(bh) * nb * (k > 0 ? k : 1) * 4));
   w.sel = reinterpret_cast<uint32_t*>(take(size_t(bh) * nb * words * 4));
+  w.pairs = reinterpret_cast<int32_t*>(take(size_t(bh) * ((nb + 1) / 2) * 2 * 4));
   w.partial = reinterpret_cast<float*>(take(static_cast<size_t>(stats_partial_bytes(bh, nb))));
   w.total = off;
   return w;
@@ -279,9 +301,19 @@ int b2_pisa_route(const void* qc, int32_t qc_dtype, const float* kc, int32_t kc_
   return ok();
 }
 
+int b2_pisa_pair(const uint32_t* sel_bits, int32_t batch_heads, int32_t blocks, int32_t* pairs, void* stream) {
+  if (!sel_bits || !pairs) return fail(B2_ERR_INVALID, "pairing pointers must be non-NULL");
+  if (batch_heads <= 0 || blocks <= 0) return fail(B2_ERR_INVALID, "pairing sizes must be positive");
+  if (blocks > 448) return fail(B2_ERR_UNSUPPORTED, "pairing supports at most 448 blocks");
+  const cudaError_t err = launch_pair(sel_bits, batch_heads, blocks, pairs, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "PISA pairing launch");
+  return ok();
+}
+
 int b2_pisa_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out,
-                      const int32_t* indices, int32_t exact_blocks, const uint32_t* sel_bits, const void* kc_bf16,
-                      const void* vc_bf16, const void* h_bf16, float scale, float* lse, void* stream) {
+                      const int32_t* indices, int32_t exact_blocks, const uint32_t* sel_bits, const int32_t* pairs,
+                      const void* kc_bf16, const void* vc_bf16, const void* h_bf16, float scale, float* lse,
+                      void* stream) {
   int rc = check_qkv_o(q, k, v, out, true);
   if (rc) return rc;
   if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA attention supports bfloat16 and float16");
@@ -293,6 +325,7 @@ int b2_pisa_attention(const b2_view* q, const b2_view* k, const b2_view* v, cons
     return fail(B2_ERR_INVALID, "the tail needs centroid values and selection bits");
   AttnParams p = base_params(q, k, v, out, scale);
   p.mode = 1;
+  p.pairs = pairs;
   p.indices = indices;
   p.nsel = exact_blocks;
   p.sel_bits = sel_bits;
@@ -356,8 +389,14 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
     err = cudaMemsetAsync(w.sel, 0, size_t(bh) * nb * words * 4, st);
     if (err != cudaSuccess) return cuda_fail(err, "selection reset");
   }
+  const bool paired = exact_blocks > 0 && nb <= 448;  // overlap matrix must fit in shared memory
+  if (paired) {
+    err = launch_pair(w.sel, bh, nb, w.pairs, st);
+    if (err != cudaSuccess) return cuda_fail(err, "PISA pairing launch");
+  }
   AttnParams p = base_params(q, k, v, out, scale);
   p.mode = 1;
+  p.pairs = paired ? w.pairs : nullptr;
   p.indices = w.indices;
   p.nsel = exact_blocks;
   p.sel_bits = w.sel;

@@ -73,6 +73,10 @@ template <> struct Cvt<__half> {
   }
 };
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device)
+// and size: later launches skip the driver call.
+cudaError_t ensure_smem(const void* kernel, int bytes);
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -81,8 +81,7 @@ fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal) {
 cudaError_t launch_fixed_f32(const Rows& q, const Rows& k, const Rows& v, const Rows& o, int batch_heads,
                              float scale, int causal, cudaStream_t stream) {
   const size_t smem = sizeof(float) * (3 * kBlock * (q.dim + 1) + kBlock * 65);
-  cudaError_t err = cudaFuncSetAttribute(fixed_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+  cudaError_t err = ensure_smem(reinterpret_cast<const void*>(fixed_f32_kernel), static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   dim3 grid((q.tokens + kBlock - 1) / kBlock, batch_heads);
   fixed_f32_kernel<<<grid, kFThreads, smem, stream>>>(q, k, v, o, scale, causal);

@@ -21,6 +21,7 @@ struct AttnParams {
   float* lse;
   int causal;
   long long* trace;
+  const int32_t* pairs;  // optional [BH][ceil(nq/2)][2] query-block pairing (-1: single)
 };
 // Arguments of the tcgen05 attention kernel (see attn_umma.cu).
 struct UmmaArgs {
@@ -38,12 +39,14 @@ struct UmmaArgs {
   Rows o;
   float* lse;
   int* status;
+  const int32_t* pairs;
   long long* trace;  // optional clock64 timeline of CTA (0,0): [tile][6] + start
 };
 bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const b2_view& o);
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,
                              const AttnParams& p, int* status, cudaStream_t stream, bool* launched);
 int* device_status_ptr();
+cudaError_t launch_pair(const uint32_t* sel_bits, int batch_heads, int blocks, int32_t* pairs, cudaStream_t stream);
 cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype, int mode, int batch_heads,
                          int blocks, void* q_centroids, float* k_centroids, void* v_stats, float* h_sum,
                          float* h_norm, void* h_half, float* partial, cudaStream_t stream);

@@ -272,7 +272,7 @@ cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype,
 #define B2_STATS_LAUNCH(T, M)                                                                              \
   do {                                                                                                     \
     auto kern = stats_kernel<T, M>;                                                                        \
-    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
+    err = ensure_smem(reinterpret_cast<const void*>(kern), static_cast<int>(smem)); \
     if (err != cudaSuccess) return err;                                                                    \
     kern<<<grid, kStatsThreads, smem, stream>>>(q, k, v, blocks, group, q_centroids, k_centroids, v_stats, \
                                                 h_norm, partial);                                          \

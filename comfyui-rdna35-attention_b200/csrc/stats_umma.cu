@@ -472,7 +472,7 @@ cudaError_t launch_stats_umma(const b2_view& q, const b2_view& k, const b2_view&
   cudaError_t err;
 #define B2_SU_LAUNCH(BF, MODE)                                                                                  \
   do {                                                                                                         \
-    err = cudaFuncSetAttribute(stats_umma_kernel<BF, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)); \
+    err = ensure_smem(reinterpret_cast<const void*>(stats_umma_kernel<BF, MODE>), int(smem)); \
     if (err != cudaSuccess) return err;                                                                        \
     stats_umma_kernel<BF, MODE><<<grid, kThreads, smem, stream>>>(qm, km, vm, a);                             \
   } while (0)

@@ -147,12 +147,22 @@ int b2_pisa_route(const void* qc, int32_t qc_dtype, const float* kc,
  * pisa_kernels.cu:296-340).  The output view may be tiled (raster write).
  * kc_bf16/vc_bf16: [BH,nb,D] centroid rows in the input's 16-bit type
  * (kc NULL: no tail); h_bf16 [BH,D,D] in the same type or NULL to skip the
- * correction; lse: [BH,T] FP32 or NULL.  q/k/v/out share [B,H,T,D=128]. */
+ * correction; lse: [BH,T] FP32 or NULL; pairs: b2_pisa_pair output or NULL
+ * (query blocks 2p, 2p+1 share a CTA).  q/k/v/out share [B,H,T,D=128]. */
 int b2_pisa_attention(const b2_view* q, const b2_view* k, const b2_view* v,
                       const b2_view* out, const int32_t* indices,
                       int32_t exact_blocks, const uint32_t* sel_bits,
-                      const void* kc_bf16, const void* vc_bf16,
-                      const void* h_bf16, float scale, float* lse, void* stream);
+                      const int32_t* pairs, const void* kc_bf16,
+                      const void* vc_bf16, const void* h_bf16, float scale,
+                      float* lse, void* stream);
+
+/* ---- Query-block pairing for the attention CTAs: pairs[bh][p] = (a, b) with
+ * b = -1 for an unpaired block; blocks are matched greedily (ascending a) with
+ * the unpaired block of largest selection overlap, so each CTA's union of
+ * exact key blocks is small.  No counterpart in the reference (its
+ * FlexAttention visits each query block's list separately).  nb <= 448. */
+int b2_pisa_pair(const uint32_t* sel_bits, int32_t batch_heads, int32_t blocks,
+                 int32_t* pairs, void* stream);
 
 /* ---- Whole PISA forward in one call: stats, routing, fused attention.
  * stats_mode B2_STATS_HYD: rdna35_pisa_ck forward / forward_spatial_bhtd
