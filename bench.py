@@ -43,6 +43,10 @@ EXACT_FLOP = 4.0 * B * H * NB * EXACT * 64 * 64 * D       # 222.3 GFLOP
 TAIL_FLOP = 4.0 * B * H * T * NB * D                      # 21.7 GFLOP (q.kc and p.vc)
 CORR_FLOP = 2.0 * B * H * T * D * D                       # 9.66 GFLOP
 STATS_BYTES = 3 * B * H * T * D * 2                       # q/k/v read once
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
+# of this workload (profiles/attn_umma_anima.md, profiles/stats_umma_anima.md)
+ATTN_TRAFFIC = 290.8e6
+STATS_TRAFFIC = 241.6e6
 CONFIG = {
     "workload": "anima_pisa_hyd_spatial",
     "batch": B, "heads": H, "tokens": T, "head_dim": D, "exact_blocks": EXACT, "blocks": NB,
@@ -249,11 +253,12 @@ def run_b200(args) -> None:
         "kernel": "attn_kernel (fused exact + tail + correction)",
         "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16"], "unit": "TFLOP/s",
         "frac": round(achieved / peaks["bf16"], 4), "peak_source": peaks["source"] + " bf16 burst",
-        "traffic": args.traffic,
+        "traffic": args.traffic if args.traffic is not None else ATTN_TRAFFIC,
         "stats_kernel": {
             "bound": "hbm", "achieved": round(STATS_BYTES / (comp["stats_ms"] * 1e-3) / 1e9, 1),
             "peak": peaks["hbm"], "unit": "GB/s",
             "frac": round(STATS_BYTES / (comp["stats_ms"] * 1e-3) / 1e9 / peaks["hbm"], 4),
+            "traffic": STATS_TRAFFIC,
         },
         "component_ms": comp,
     }
