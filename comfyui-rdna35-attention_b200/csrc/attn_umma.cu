@@ -411,9 +411,6 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 3] = clock64();
       tc_fence_after();
       const uint32_t s_addr = o_base + 128 + 64 * sb;
-      // logits in the log2 domain: x = s * scale_log2 (+ log2 len for the tail),
-      // masked -> -inf.  Two passes over the S columns (32 at a time) keep the
-      // register footprint small: max first, then exp2 + P.
       const int klen = t.tail ? 64 : min(64, tk_ - t.blk * 64);
       const bool plain = !t.tail && klen == 64 && !causal_;
       // masked columns of this tile as two 32-bit words (bit c = column c),
@@ -445,32 +442,44 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       const float last_bias = log2_last_;
       float alpha = 1.f;
       bool rescale = false;
+      // the row's 64 logits are read from TMEM once; the S buffer goes back
+      // to the MMA issuer as soon as they are in registers
+      uint32_t v[64];
       if (active) {
-        float mx = -INFINITY;
-#pragma unroll 1
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t v[32];
-          tmem_ld32(s_addr + 32 * h2, v);
-          tmem_wait_ld();
-          if (h2 == 0 && trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 2] = clock64();
-          if (plain) {
-            float m0 = fmaxf(__uint_as_float(v[0]), __uint_as_float(v[1]));
-            float m1 = fmaxf(__uint_as_float(v[2]), __uint_as_float(v[3]));
+        tmem_ld32(s_addr, v);
+        tmem_ld32(s_addr + 32, v + 32);
+        tmem_wait_ld();
+      }
+      if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 2] = clock64();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&m.s_free[wg][sb]);
+      // logits in the log2 domain: x = s * scale_log2 (+ log2 len for the
+      // tail), masked -> -inf.  Plain tiles keep raw s and fold the scale
+      // into the exp2 argument.
+      float mul = scale_log2_;
+      if (active) {
+        float mx;
+        if (plain) {
+          float m0 = fmaxf(__uint_as_float(v[0]), __uint_as_float(v[1]));
+          float m1 = fmaxf(__uint_as_float(v[2]), __uint_as_float(v[3]));
 #pragma unroll
-            for (int c = 4; c < 32; c += 4) {
-              m0 = max3(m0, __uint_as_float(v[c]), __uint_as_float(v[c + 1]));
-              m1 = max3(m1, __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
-            }
-            mx = fmaxf(mx, fmaxf(m0, m1) * scale_log2_);
-          } else {
-            const uint32_t bw = h2 ? bad1 : bad0;
-            const int lc = lastc - 32 * h2;
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const float x = fmaf(__uint_as_float(v[c]), scale_log2_, c == lc ? last_bias : bias);
-              mx = fmaxf(mx, ((bw >> c) & 1u) ? -INFINITY : x);
-            }
+          for (int c = 4; c < 64; c += 4) {
+            m0 = max3(m0, __uint_as_float(v[c]), __uint_as_float(v[c + 1]));
+            m1 = max3(m1, __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
           }
+          mx = fmaxf(m0, m1) * scale_log2_;
+        } else {
+          mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            const uint32_t bw = c < 32 ? bad0 : bad1;
+            const float x = fmaf(__uint_as_float(v[c]), scale_log2_, c == lastc ? last_bias : bias);
+            const float xm = ((bw >> (c & 31)) & 1u) ? -INFINITY : x;
+            v[c] = __float_as_uint(xm);
+            mx = fmaxf(mx, xm);
+          }
+          mul = 1.f;
         }
         const float mnew = fmaxf(mrun, mx);
         if (mrun == -INFINITY) {
@@ -505,37 +514,19 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       if (active && mrun != -INFINITY) {
         const float neg = -mrun;
         float s0 = 0.f, s1 = 0.f;
-#pragma unroll 1
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t v[32];
-          tmem_ld32(s_addr + 32 * h2, v);
-          tmem_wait_ld();
-          float mul = scale_log2_;
-          if (!plain) {
-            const uint32_t bw = h2 ? bad1 : bad0;
-            const int lc = lastc - 32 * h2;
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const float x = fmaf(__uint_as_float(v[c]), scale_log2_, c == lc ? last_bias : bias);
-              v[c] = __float_as_uint(((bw >> c) & 1u) ? -INFINITY : x);
-            }
-            mul = 1.f;
+        for (int chunk = 0; chunk < 8; ++chunk) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float x0, x1;
+            fma2(x0, x1, __uint_as_float(v[8 * chunk + 2 * e]), __uint_as_float(v[8 * chunk + 2 * e + 1]), mul, neg);
+            const float p0 = ex2(x0);
+            const float p1 = ex2(x1);
+            add2(s0, s1, p0, p1);
+            w4[e] = Cvt<T>::pack2(p0, p1);
           }
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float x0, x1;
-              fma2(x0, x1, __uint_as_float(v[8 * c + 2 * e]), __uint_as_float(v[8 * c + 2 * e + 1]), mul, neg);
-              const float p0 = ex2(x0);
-              const float p1 = ex2(x1);
-              add2(s0, s1, p0, p1);
-              w4[e] = Cvt<T>::pack2(p0, p1);
-            }
-            const int chunk = 4 * h2 + c;
-            *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-          }
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
         const float sum = s0 + s1;
         lrun = lrun * alpha + sum;
@@ -544,9 +535,6 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
 #pragma unroll
         for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(prow + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&m.s_free[wg][sb]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();

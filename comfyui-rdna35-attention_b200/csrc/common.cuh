@@ -58,6 +58,12 @@ inline Rows make_rows(const b2_view& v) {
 template <typename T> struct Cvt;
 template <> struct Cvt<__nv_bfloat16> {
   static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  // widen a packed pair with integer ops (bf16 is the top half of an f32),
+  // keeping the conversion pipe free
+  static __device__ __forceinline__ void unpack2(uint32_t w, float& lo, float& hi) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xFFFF0000u);
+  }
   static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
   static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -66,6 +72,11 @@ template <> struct Cvt<__nv_bfloat16> {
 };
 template <> struct Cvt<__half> {
   static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ void unpack2(uint32_t w, float& lo, float& hi) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    lo = f.x;
+    hi = f.y;
+  }
   static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
   static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);

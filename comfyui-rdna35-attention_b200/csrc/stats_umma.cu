@@ -281,16 +281,18 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const uint32_t w = *reinterpret_cast<const uint32_t*>(base + (rr + u) * 128 + ((chunk ^ u) << 4));
-              const T* pr = reinterpret_cast<const T*>(&w);
-              s0 += Cvt<T>::to_f(pr[0]);
-              s1 += Cvt<T>::to_f(pr[1]);
+              float f0, f1;
+              Cvt<T>::unpack2(w, f0, f1);
+              s0 += f0;
+              s1 += f1;
             }
           }
           for (int r = full_rows; r < len; ++r) {
             const uint32_t w = *reinterpret_cast<const uint32_t*>(base + r * 128 + ((chunk ^ (r & 7)) << 4));
-            const T* pr = reinterpret_cast<const T*>(&w);
-            s0 += Cvt<T>::to_f(pr[0]);
-            s1 += Cvt<T>::to_f(pr[1]);
+            float f0, f1;
+            Cvt<T>::unpack2(w, f0, f1);
+            s0 += f0;
+            s1 += f1;
           }
           const int64_t o = (int64_t(bh) * a.blocks + blk) * 128 + col;
           if (MODE == B2_STATS_HYD) {
@@ -333,18 +335,20 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
           const uint32_t off = half * 8192 + r * 128 + ((cc ^ (r & 7)) << 4);
           const int c0 = half * 64 + cc * 8;
           const uint4 raw = *reinterpret_cast<const uint4*>(st + kTile + off);
-          const T* kv = reinterpret_cast<const T*>(&raw);
+          const uint32_t kw[4] = {raw.x, raw.y, raw.z, raw.w};
           uint32_t hw[4], lw[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             float x0 = 0.f, x1 = 0.f;
             if (r < len) {
-              x0 = Cvt<T>::to_f(kv[2 * e]) - m.kmean[c0 + 2 * e];
-              x1 = Cvt<T>::to_f(kv[2 * e + 1]) - m.kmean[c0 + 2 * e + 1];
+              Cvt<T>::unpack2(kw[e], x0, x1);
+              x0 -= m.kmean[c0 + 2 * e];
+              x1 -= m.kmean[c0 + 2 * e + 1];
             }
             hw[e] = Cvt<T>::pack2(x0, x1);
-            const T* hp = reinterpret_cast<const T*>(&hw[e]);
-            lw[e] = Cvt<T>::pack2(x0 - Cvt<T>::to_f(hp[0]), x1 - Cvt<T>::to_f(hp[1]));
+            float h0, h1;
+            Cvt<T>::unpack2(hw[e], h0, h1);
+            lw[e] = Cvt<T>::pack2(x0 - h0, x1 - h1);
           }
           *reinterpret_cast<uint4*>(hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
           if (with_lo) *reinterpret_cast<uint4*>(lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);

@@ -62,7 +62,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const long long start = clock64();
   while (true) {
     if (*abort_flag) return false;
-    __nanosleep(20);  // back off so waiting warps leave issue slots to the math warps
+#ifndef B2_WAIT_SLEEP_NS
+#define B2_WAIT_SLEEP_NS 0
+#endif
+    if (B2_WAIT_SLEEP_NS > 0) __nanosleep(B2_WAIT_SLEEP_NS);  // back off so waiting warps leave issue slots
     if (mbar_try_wait(bar, parity)) return true;
     if (clock64() - start > (1ll << 31)) {
       *abort_flag = 1;
