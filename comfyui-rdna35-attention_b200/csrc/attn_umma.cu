@@ -13,22 +13,28 @@
 //   * fixed block (mode DIAG): each query block's own key block
 //     (triton_kernel.py:53-100, optional causal mask).
 //
-// Warp roles (320 threads, one CTA per SM):
-//   warp 0    TMA producer: Q pair once, then K/V (or centroid) tiles into a
-//             5-stage ring, finally H (first-order operand) for the correction
+// Warp roles (352 threads, one CTA per SM):
+//   warp 0    TMA producer: Q pair once, then K (or centroid) tiles into a
+//             6-stage ring, finally H (first-order operand) for the correction
+//   warp 10   TMA producer of the V tiles (own 6-stage ring)
 //   warp 1    TMEM owner (512 columns) + single-thread MMA issuer:
-//             S(j) = Q K(j)^T  -> TMEM S of warpgroup j%2 (128 x 64 FP32)
-//             O   += P(j) V(j) -> TMEM O of warpgroup j%2 (128 x 128 FP32)
+//             S(j) = Q K(j)^T  -> TMEM S buffer of warpgroup j%2 (128 x 64 FP32,
+//                                 two buffers per warpgroup)
+//             O   += P(j) V(j) -> TMEM O of warpgroup j%2 (128 x 128 FP32),
+//                                 P read from TMEM (tcgen05.mma A operand)
 //             C    = Q H       -> TMEM (reuses warpgroup 0's S columns)
+//             S(j) reuses the buffer of P(j-4), so it is issued only after
+//             that P.V has completed; otherwise S and P.V go out as their
+//             operands arrive.
 //   warps 2-5 / 6-9  two softmax warpgroups taking alternate key tiles (split
 //             K inside the CTA): thread r owns query row r (TMEM lane r);
-//             reads S with tcgen05.ld, computes exp2 of the scaled logits
-//             with packed f32x2 arithmetic, keeps a lazy running max (O is
-//             rescaled in TMEM only when the max grows by more than 2^8), and
-//             writes P as 16-bit into its own 128-byte-swizzled shared tile.
-//             At the end the two partial softmaxes are merged and
-//             (O + tail_mass * corr_scale * C) / l is stored, each warpgroup
-//             writing half of the columns.
+//             reads its 64 logits with one tcgen05.ld pair, computes exp2 of
+//             the scaled logits with packed f32x2 arithmetic, keeps a lazy
+//             running max (O is rescaled in TMEM only when the max grows by
+//             more than 2^8), and writes P as 16-bit pairs back over the S
+//             columns with tcgen05.st.  At the end the two partial softmaxes
+//             are merged and (O + tail_mass * corr_scale * C) / l is stored,
+//             each warpgroup writing half of the columns.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -43,11 +49,10 @@ namespace {
 using namespace umma;
 
 constexpr int kThreads = 352;  // K producer, MMA, 2 softmax warpgroups, V producer
-constexpr int kStages = 5;
+constexpr int kStages = 6;
 constexpr int kMaxList = 192;  // union of two selected lists
 constexpr int kMaxSelWords = 32;
 constexpr uint32_t kQBytes = 128 * 128 * 2;
-constexpr uint32_t kPBytes = 128 * 64 * 2;
 constexpr uint32_t kSlotBytes = 64 * 128 * 2;  // one K or V tile (two 8 KB d-halves)
 
 struct __align__(8) Misc {
@@ -57,9 +62,9 @@ struct __align__(8) Misc {
   uint64_t v_full[kStages];
   uint64_t v_empty[kStages];
   uint64_t s_full[2][2];
-  uint64_t s_free[2][2];
-  uint64_t p_full[2];
-  uint64_t pv_done[2];
+  uint64_t p_full[2][2];  // [warpgroup][S buffer]: a warpgroup may run one tile ahead of the P.V issue
+  uint64_t pv_done[2][2];  // [warpgroup][S buffer]
+  uint64_t pv_all;         // every P.V complete (before C reuses warpgroup 0's S columns)
   uint64_t c_full;
   uint64_t mma_done;
   uint32_t tmem;
@@ -72,8 +77,7 @@ struct __align__(8) Misc {
 
 struct SmemLayout {
   static constexpr uint32_t q = 0;                 // [2 d-halves][128 rows][128 B]
-  static constexpr uint32_t p = q + kQBytes;       // [2 warpgroups][128 rows][128 B]
-  static constexpr uint32_t k = p + 2 * kPBytes;   // [stages][2 d-halves x 8 KB]
+  static constexpr uint32_t k = q + kQBytes;       // [stages][2 d-halves x 8 KB]
   static constexpr uint32_t v = k + kStages * kSlotBytes;
   static constexpr uint32_t misc = v + kStages * kSlotBytes;
   static constexpr uint32_t total = misc + sizeof(Misc);
@@ -149,6 +153,8 @@ __device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
 }
 
 // S(j) = Q K(j)^T into the S buffer of warpgroup j%2; frees K slot on completion.
+// The buffer last held P(j-4): the caller issues S(j) only once that P.V has
+// completed (it reads P from these TMEM columns).
 template <bool BF16>
 __device__ __forceinline__ bool issue_s(Misc& m, char* k_s, uint32_t q_addr, uint32_t tmem, const UmmaArgs& a,
                                         volatile int* abort_flag, int j, long long* trace) {
@@ -157,7 +163,6 @@ __device__ __forceinline__ bool issue_s(Misc& m, char* k_s, uint32_t q_addr, uin
   const int i = j >> 1;
   const int sb = i & 1;
   if (!mbar_wait(&m.k_full[s], (j / kStages) & 1, abort_flag, a.status, 4)) return false;
-  if (!mbar_wait(&m.s_free[w][sb], ((i >> 1) & 1) ^ 1, abort_flag, a.status, 5)) return false;
   tc_fence_after();
   if (trace && j < 256) trace[6 * j + 1] = clock64();
   const uint32_t idesc_s = idesc_f16(128, 64, BF16, false, false);
@@ -173,25 +178,36 @@ __device__ __forceinline__ bool issue_s(Misc& m, char* k_s, uint32_t q_addr, uin
   return true;
 }
 
-// O(w) += P(w) V(jj): the P.V product of key tile jj (warpgroup w = jj % 2).
+// D[tmem] (+)= A[tmem] * B[smem]: A is M x K, 16-bit pairs packed per 32-bit
+// column (lane = row), K = 16 per instruction = 8 columns.
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// O(w) += P(jj) V(jj) for key tile jj (warpgroup w = jj % 2); P is read from
+// TMEM, where the softmax wrote it over the tile's S columns.
 template <bool BF16>
 __device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, const UmmaArgs& a,
                                          volatile int* abort_flag, int jj) {
   const int w = jj & 1;
   const int i = jj >> 1;
-  if (!mbar_wait(&m.p_full[w], i & 1, abort_flag, a.status, 2)) return false;
+  const uint32_t p_tmem = tmem + w * 256 + 128 + 64 * (i & 1);
+  if (!mbar_wait(&m.p_full[w][i & 1], (i >> 1) & 1, abort_flag, a.status, 2)) return false;
   if (!mbar_wait(&m.v_full[jj % kStages], (jj / kStages) & 1, abort_flag, a.status, 12)) return false;
   tc_fence_after();
   const uint32_t idesc_o = idesc_f16(128, 128, BF16, false, true);
-  const uint32_t p_addr = smem_u32(smem + SmemLayout::p + w * kPBytes);
   const uint32_t v_addr = smem_u32(smem + SmemLayout::v + (jj % kStages) * kSlotBytes);
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
-    const uint64_t da = smem_desc_sw128(p_addr + kk * 32, 16, 1024);
     const uint64_t db = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
-    mma_ss(tmem + w * 256, da, db, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+    mma_ts(tmem + w * 256, p_tmem + kk * 8, db, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
   }
-  mma_commit(&m.pv_done[w]);
+  mma_commit(&m.pv_done[w][i & 1]);
   mma_commit(&m.v_empty[jj % kStages]);
   return true;
 }
@@ -240,13 +256,15 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     for (int w = 0; w < 2; ++w) {
       for (int b = 0; b < 2; ++b) {
         mbar_init(&m.s_full[w][b], 1);
-        mbar_init(&m.s_free[w][b], 4);
       }
-      mbar_init(&m.p_full[w], 4);
-      mbar_init(&m.pv_done[w], 1);
+      mbar_init(&m.p_full[w][0], 4);
+      mbar_init(&m.p_full[w][1], 4);
+      mbar_init(&m.pv_done[w][0], 1);
+      mbar_init(&m.pv_done[w][1], 1);
     }
     mbar_init(&m.c_full, 1);
     mbar_init(&m.mma_done, 1);
+    mbar_init(&m.pv_all, 1);
     int nlist = 0;
     if (a.mode == 1) {
       const int32_t* la = a.indices + (int64_t(bh) * a.nqb + qa) * a.nsel;
@@ -349,15 +367,48 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       const uint32_t q_addr = smem_u32(q_s);
-      // Order: S(0..3), then for each tile j: P.V(j) followed by S(j+4).  Each
-      // warpgroup has two S buffers, so S(j+2) is ready before it finishes
-      // the softmax of tile j; K slots are released as soon as S completes.
+      // S(j) may go out once the P.V of tile j-4 (same S buffer) has completed
+      // and its K tile is in; P.V(j) once P(j) and V(j) are.  Each warpgroup
+      // has two S buffers, so S(j+2) is ready before it finishes the softmax
+      // of tile j.  Whichever is ready first is issued, S preferred.
       bool ok = mbar_wait(&m.q_full, 0, abort_flag, a.status, 3);
-      int issued = 0;
-      while (ok && issued < n && issued < 4) ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, issued++, trace);
-      for (int j = 0; ok && j < n; ++j) {
-        ok = issue_pv<BF16>(m, smem, tmem, a, abort_flag, j);
-        if (ok && issued < n) ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, issued++, trace);
+      int ns = 0, npv = 0;
+      const long long start = clock64();
+      while (ok && npv < n) {
+        bool did = false;
+        if (ns < n) {
+          const int w = ns & 1, i = ns >> 1;
+          const bool buf_free = ns < 4 || (ns - 4 < npv && mbar_try_wait(&m.pv_done[w][i & 1], ((i - 2) >> 1) & 1));
+          if (buf_free && mbar_try_wait(&m.k_full[ns % kStages], (ns / kStages) & 1)) {
+            ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, ns, trace);
+            ++ns;
+            did = true;
+          }
+        }
+        if (!did && ok && npv < ns) {
+          const int w = npv & 1, i = npv >> 1;
+          if (mbar_try_wait(&m.p_full[w][i & 1], (i >> 1) & 1) &&
+              mbar_try_wait(&m.v_full[npv % kStages], (npv / kStages) & 1)) {
+            ok = issue_pv<BF16>(m, smem, tmem, a, abort_flag, npv);
+            ++npv;
+            did = true;
+          }
+        }
+        if (!did) {
+          if (*abort_flag) {
+            ok = false;
+          } else if (clock64() - start > (1ll << 33)) {
+            // far beyond any legitimate CTA duration
+            *abort_flag = 1;
+            atomicCAS(a.status, kStatusOk, (kStatusTimeout << 8) | 23);
+            ok = false;
+          }
+        }
+      }
+      if (ok && a.has_corr) {
+        // C overwrites warpgroup 0's S columns: every P.V must have read its P
+        mma_commit(&m.pv_all);
+        ok = mbar_wait(&m.pv_all, 0, abort_flag, a.status, 24);
       }
       if (ok && a.has_corr) {
         // C = Q H as two N=64 products, one per 64-column half of H
@@ -397,7 +448,6 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     float mrun = -INFINITY, lrun = 0.f, tmass = 0.f;
     const int nb_ = a.nb, causal_ = a.causal, tk_ = a.tk;
     const float log2_last_ = a.log2_last, scale_log2_ = a.scale_log2;
-    char* prow = smem + SmemLayout::p + wg * kPBytes + (row >> 3) * 1024 + (row & 7) * 128;
     int i = 0;
     bool ok = true;
     for (int j = wg; j < n; j += 2, ++i) {
@@ -442,8 +492,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       const float last_bias = log2_last_;
       float alpha = 1.f;
       bool rescale = false;
-      // the row's 64 logits are read from TMEM once; the S buffer goes back
-      // to the MMA issuer as soon as they are in registers
+      // the row's 64 logits are read from TMEM once; P goes back over them
       uint32_t v[64];
       if (active) {
         tmem_ld32(s_addr, v);
@@ -451,9 +500,6 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         tmem_wait_ld();
       }
       if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 2] = clock64();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&m.s_free[wg][sb]);
       // logits in the log2 domain: x = s * scale_log2 (+ log2 len for the
       // tail), masked -> -inf.  Plain tiles keep raw s and fold the scale
       // into the exp2 argument.
@@ -491,12 +537,13 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         }
       }
       if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 4] = clock64();
-      // the P tile and O of this warpgroup are free once its previous P.V is done
-      if (i >= 1 && !mbar_wait(&m.pv_done[wg], (i - 1) & 1, abort_flag, a.status, 9)) {
-        ok = false;
-        break;
-      }
       if (__any_sync(0xffffffffu, rescale)) {
+        // O may be rescaled once this warpgroup's previous P.V is done (the
+        // one before it completed ahead of S(j))
+        if (i >= 1 && !mbar_wait(&m.pv_done[wg][(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, a.status, 9)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
 #pragma unroll 1
         for (int c0 = 0; c0 < 128; c0 += 32) {
@@ -509,40 +556,36 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         }
         tmem_wait_st();
       }
-      // P = exp2(x - m) -> 16-bit, straight into the 128-byte swizzled K-major
-      // tile (16-byte chunk c of row r lives at chunk c ^ (r % 8))
+      // P = exp2(x - m) -> 16-bit pairs, written back over the first 32 S
+      // columns of the buffer (the A operand of P.V)
       if (active && mrun != -INFINITY) {
         const float neg = -mrun;
         float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-        for (int chunk = 0; chunk < 8; ++chunk) {
-          uint32_t w4[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float x0, x1;
-            fma2(x0, x1, __uint_as_float(v[8 * chunk + 2 * e]), __uint_as_float(v[8 * chunk + 2 * e + 1]), mul, neg);
-            const float p0 = ex2(x0);
-            const float p1 = ex2(x1);
-            add2(s0, s1, p0, p1);
-            w4[e] = Cvt<T>::pack2(p0, p1);
-          }
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (row & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        for (int c = 0; c < 64; c += 2) {
+          float x0, x1;
+          fma2(x0, x1, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), mul, neg);
+          const float p0 = ex2(x0);
+          const float p1 = ex2(x1);
+          add2(s0, s1, p0, p1);
+          v[c / 2] = Cvt<T>::pack2(p0, p1);
         }
         const float sum = s0 + s1;
         lrun = lrun * alpha + sum;
         tmass = tmass * alpha + (t.tail ? sum : 0.f);
       } else {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(prow + (c << 4)) = make_uint4(0u, 0u, 0u, 0u);
+        for (int c = 0; c < 32; ++c) v[c] = 0u;
       }
-      fence_proxy_async_smem();
+      tmem_st32(s_addr, v);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&m.p_full[wg]);
+      if (lane == 0) mbar_arrive(&m.p_full[wg][sb]);
       if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 5] = clock64();
     }
     // ---- merge the two partial softmaxes, add the correction, store
-    if (ok && i >= 1) ok = mbar_wait(&m.pv_done[wg], (i - 1) & 1, abort_flag, a.status, 10);
+    if (ok && i >= 1) ok = mbar_wait(&m.pv_done[wg][(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, a.status, 10);
     // partial statistics [m | l | tail mass] x 128 rows per warpgroup go into
     // the V ring (every P.V has completed once both warpgroups get here)
     named_barrier_sync(1, 256);
