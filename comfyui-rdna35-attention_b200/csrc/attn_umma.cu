@@ -378,8 +378,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         bool did = false;
         if (ns < n) {
           const int w = ns & 1, i = ns >> 1;
-          const bool buf_free = ns < 4 || (ns - 4 < npv && mbar_try_wait(&m.pv_done[w][i & 1], ((i - 2) >> 1) & 1));
-          if (buf_free && mbar_try_wait(&m.k_full[ns % kStages], (ns / kStages) & 1)) {
+          const bool buf_free = ns < 4 || (ns - 4 < npv && mbar_test_wait(&m.pv_done[w][i & 1], ((i - 2) >> 1) & 1));
+          if (buf_free && mbar_test_wait(&m.k_full[ns % kStages], (ns / kStages) & 1)) {
             ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, ns, trace);
             ++ns;
             did = true;
@@ -387,8 +387,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         }
         if (!did && ok && npv < ns) {
           const int w = npv & 1, i = npv >> 1;
-          if (mbar_try_wait(&m.p_full[w][i & 1], (i >> 1) & 1) &&
-              mbar_try_wait(&m.v_full[npv % kStages], (npv / kStages) & 1)) {
+          if (mbar_test_wait(&m.p_full[w][i & 1], (i >> 1) & 1) &&
+              mbar_test_wait(&m.v_full[npv % kStages], (npv / kStages) & 1)) {
             ok = issue_pv<BF16>(m, smem, tmem, a, abort_flag, npv);
             ++npv;
             did = true;
