@@ -6,10 +6,11 @@
 // +inf sink, topk then ascending sort) and generic_pisa.py:172-184 (FP32
 // centroids, no bias).  Ties at the cut resolve to the lower block index.
 //
-// One CTA owns 16 query blocks: scores are built in shared memory 128 key
-// centroids at a time (staged transposed so the 16 column lanes of a row read
-// consecutive words), then each warp runs k rounds of warp-wide argmax for two
-// rows.
+// One CTA owns 16 query blocks.  BF16 centroids (HYD): scores on the tensor
+// cores (mma.sync, FP32 accumulate) straight from global memory; FP32
+// centroids (generic): FP32 FMAs over centroids staged transposed in shared
+// memory.  Then each warp selects the top-k of two rows with k rounds of
+// warp max reductions (redux.sync) on order-preserving integer keys.
 #include "common.cuh"
 
 namespace b2 {
@@ -20,6 +21,26 @@ constexpr int kThreadsR = 256;  // 16 rows x 16 column lanes
 constexpr int kColChunk = 256;  // key centroids staged per pass
 constexpr int kDim = 128;
 constexpr int kMaxBlocks = 1024;
+
+// Float -> uint32 whose unsigned order is the float order.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// D(16x8, f32) += A(16x16, bf16, row-major) * B(16x8, bf16, col-major)
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 
 // Scores of kRows query blocks against every key block, then per-row top-k.
 // Thread (r, cl) accumulates columns cl + 16*i of row r over d in order
@@ -32,70 +53,116 @@ route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict
   const int words = (blocks + 31) >> 5;
   const int chunk = min(kColChunk, (blocks + 15) & ~15);  // columns staged per pass
   const int pitch = chunk + 1;
-  float* qrow = rs;                        // [16][128]
-  float* kct = qrow + kRows * kDim;        // [128][pitch]
-  float* scores = kct + kDim * pitch;      // [16][blocks]
+  const bool mma_path = !qc_is_f32 && kc_round_bf16;
+  float* qrow = rs;                        // [16][128]          (FP32 path)
+  float* kct = qrow + kRows * kDim;        // [128][pitch]       (FP32 path)
+  float* scores = mma_path ? rs : kct + kDim * pitch;  // [16][blocks]
   (void)dim;
   const int bh = blockIdx.y;
   const int row0 = blockIdx.x * kRows;
   const int t = threadIdx.x;
   const int r = t >> 4;
   const int cl = t & 15;
-  for (int idx = t; idx < kRows * kDim; idx += kThreadsR) {
-    const int rr = idx >> 7;
-    const int d = idx & (kDim - 1);
-    const int qi = row0 + rr;
-    float val = 0.f;
-    if (qi < blocks) {
-      const int64_t off = (int64_t(bh) * blocks + qi) * kDim + d;
-      val = qc_is_f32 ? static_cast<const float*>(qc)[off]
-                      : __bfloat162float(static_cast<const __nv_bfloat16*>(qc)[off]);
+  if (mma_path) {
+    // BF16 centroids (HYD): exact bf16 products on the tensor cores with FP32
+    // accumulation (mma.sync m16n8k16; the sum order differs from the
+    // sequential one only by FP32 rounding).  Warp w owns 8-column tiles
+    // w, w+8, ...; A (16 query rows x 128) stays in registers.
+    const int warp = t >> 5;
+    const int lane = t & 31;
+    const int g = lane >> 2;        // fragment row / column group
+    const int q2 = (lane & 3) * 2;  // fragment k pair
+    const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(qc) + int64_t(bh) * blocks * kDim;
+    uint32_t af[kDim / 16][4];
+#pragma unroll
+    for (int ks = 0; ks < kDim / 16; ++ks) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int rr = g + ((h & 1) ? 8 : 0);
+        const int kk = ks * 16 + q2 + ((h & 2) ? 8 : 0);
+        const int qi = row0 + rr;
+        af[ks][h] = qi < blocks ? *reinterpret_cast<const uint32_t*>(qb + int64_t(qi) * kDim + kk) : 0u;
+      }
     }
-    qrow[idx] = val;
-  }
-  for (int c0 = 0; c0 < blocks; c0 += chunk) {
-    __syncthreads();
-    const int ncol = min(chunk, blocks - c0);
-    // k rows read as float4 (coalesced), stored transposed
-    for (int idx = t; idx < chunk * (kDim / 4); idx += kThreadsR) {
-      const int j = idx >> 5;
-      const int d4 = (idx & 31) * 4;
-      float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < ncol) {
-        val = *reinterpret_cast<const float4*>(kc + (int64_t(bh) * blocks + c0 + j) * kDim + d4);
-        if (kc_round_bf16) {
-          val.x = __bfloat162float(__float2bfloat16_rn(val.x));
-          val.y = __bfloat162float(__float2bfloat16_rn(val.y));
-          val.z = __bfloat162float(__float2bfloat16_rn(val.z));
-          val.w = __bfloat162float(__float2bfloat16_rn(val.w));
+    const int ntiles = (blocks + 7) >> 3;
+    for (int nt = warp; nt < ntiles; nt += kThreadsR / 32) {
+      const int n = nt * 8 + g;  // key block of this lane's B fragment
+      const float* kr = kc + (int64_t(bh) * blocks + min(n, blocks - 1)) * kDim;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < kDim / 16; ++ks) {
+        const float2 lo = *reinterpret_cast<const float2*>(kr + ks * 16 + q2);
+        const float2 hi = *reinterpret_cast<const float2*>(kr + ks * 16 + q2 + 8);
+        mma_bf16_16816(d, af[ks], pack_bf16x2(lo.x, lo.y), pack_bf16x2(hi.x, hi.y));
+      }
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int rr = g + ((h & 2) ? 8 : 0);
+        const int j = nt * 8 + q2 + (h & 1);
+        if (j < blocks) {
+          float sc = d[h] * scale;
+          if (h_norm != nullptr) sc = sc + logf(h_norm[int64_t(bh) * blocks + j] + 1e-5f);
+          scores[rr * blocks + j] = sc;
         }
       }
-      kct[(d4 + 0) * pitch + j] = val.x;
-      kct[(d4 + 1) * pitch + j] = val.y;
-      kct[(d4 + 2) * pitch + j] = val.z;
-      kct[(d4 + 3) * pitch + j] = val.w;
     }
-    __syncthreads();
-    const int na = (ncol + 15) >> 4;  // accumulators in use (<= 16)
-    float acc[kColChunk / 16];
-#pragma unroll
-    for (int i = 0; i < kColChunk / 16; ++i) acc[i] = 0.f;
-    const float* qr = qrow + r * kDim;
-#pragma unroll 2
-    for (int d = 0; d < kDim; ++d) {
-      const float qv = qr[d];
-      const float* kr = kct + d * pitch + cl;
-#pragma unroll
-      for (int i = 0; i < kColChunk / 16; ++i)
-        if (i < na) acc[i] = fmaf(qv, kr[16 * i], acc[i]);
+  } else {
+    for (int idx = t; idx < kRows * kDim; idx += kThreadsR) {
+      const int rr = idx >> 7;
+      const int d = idx & (kDim - 1);
+      const int qi = row0 + rr;
+      float val = 0.f;
+      if (qi < blocks) {
+        const int64_t off = (int64_t(bh) * blocks + qi) * kDim + d;
+        val = qc_is_f32 ? static_cast<const float*>(qc)[off]
+                        : __bfloat162float(static_cast<const __nv_bfloat16*>(qc)[off]);
+      }
+      qrow[idx] = val;
     }
-#pragma unroll
-    for (int i = 0; i < kColChunk / 16; ++i) {
-      const int j = cl + 16 * i;
-      if (i < na && j < ncol) {
-        float sc = acc[i] * scale;
-        if (h_norm != nullptr) sc = sc + logf(h_norm[int64_t(bh) * blocks + c0 + j] + 1e-5f);
-        scores[r * blocks + c0 + j] = sc;
+    for (int c0 = 0; c0 < blocks; c0 += chunk) {
+      __syncthreads();
+      const int ncol = min(chunk, blocks - c0);
+      // k rows read as float4 (coalesced), stored transposed
+      for (int idx = t; idx < chunk * (kDim / 4); idx += kThreadsR) {
+        const int j = idx >> 5;
+        const int d4 = (idx & 31) * 4;
+        float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < ncol) {
+          val = *reinterpret_cast<const float4*>(kc + (int64_t(bh) * blocks + c0 + j) * kDim + d4);
+          if (kc_round_bf16) {
+            val.x = __bfloat162float(__float2bfloat16_rn(val.x));
+            val.y = __bfloat162float(__float2bfloat16_rn(val.y));
+            val.z = __bfloat162float(__float2bfloat16_rn(val.z));
+            val.w = __bfloat162float(__float2bfloat16_rn(val.w));
+          }
+        }
+        kct[(d4 + 0) * pitch + j] = val.x;
+        kct[(d4 + 1) * pitch + j] = val.y;
+        kct[(d4 + 2) * pitch + j] = val.z;
+        kct[(d4 + 3) * pitch + j] = val.w;
+      }
+      __syncthreads();
+      const int na = (ncol + 15) >> 4;  // accumulators in use (<= 16)
+      float acc[kColChunk / 16];
+  #pragma unroll
+      for (int i = 0; i < kColChunk / 16; ++i) acc[i] = 0.f;
+      const float* qr = qrow + r * kDim;
+  #pragma unroll 2
+      for (int d = 0; d < kDim; ++d) {
+        const float qv = qr[d];
+        const float* kr = kct + d * pitch + cl;
+  #pragma unroll
+        for (int i = 0; i < kColChunk / 16; ++i)
+          if (i < na) acc[i] = fmaf(qv, kr[16 * i], acc[i]);
+      }
+  #pragma unroll
+      for (int i = 0; i < kColChunk / 16; ++i) {
+        const int j = cl + 16 * i;
+        if (i < na && j < ncol) {
+          float sc = acc[i] * scale;
+          if (h_norm != nullptr) sc = sc + logf(h_norm[int64_t(bh) * blocks + c0 + j] + 1e-5f);
+          scores[r * blocks + c0 + j] = sc;
+        }
       }
     }
   }
@@ -114,26 +181,22 @@ route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict
     }
     uint32_t taken = 0;  // bit m <-> column lane + 32*m
     for (int round = 0; round < k; ++round) {
-      float best = -__int_as_float(0x7f800000);
-      int best_j = 0x7fffffff;
+      // lane's best untaken column (lowest index among equal scores), then
+      // the warp maximum and, among lanes holding it, the lowest index
+      uint32_t best = 0u;
+      uint32_t best_j = 0xffffffffu;
       for (int m = 0, j = lane; j < blocks; ++m, j += 32) {
         if (taken & (1u << m)) continue;
-        const float val = srow[j];
-        if (val > best || (val == best && j < best_j)) {
-          best = val;
+        const uint32_t key = order_key(srow[j]);
+        if (key > best) {
+          best = key;
           best_j = j;
         }
       }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-        const int oj = __shfl_xor_sync(0xffffffffu, best_j, off);
-        if (ov > best || (ov == best && oj < best_j)) {
-          best = ov;
-          best_j = oj;
-        }
-      }
-      if (best_j != 0x7fffffff && (best_j & 31) == lane) taken |= 1u << (best_j >> 5);
+      const uint32_t wmax = __reduce_max_sync(0xffffffffu, best);
+      const uint32_t wj = __reduce_min_sync(0xffffffffu, best == wmax ? best_j : 0xffffffffu);
+      if (wj == 0xffffffffu) break;
+      if ((wj & 31) == static_cast<uint32_t>(lane)) taken |= 1u << (wj >> 5);
     }
     uint32_t word = 0;
     for (int w = 0; w < words; ++w) {
@@ -191,27 +254,17 @@ __global__ void __launch_bounds__(256) pair_kernel(const uint32_t* __restrict__ 
   for (int a = 0; a < blocks; ++a) {
     const uint32_t a_used = __shfl_sync(0xffffffffu, (mine >> (a >> 5)) & 1u, a & 31);
     if (a_used) continue;
-    int best = -1, best_j = 0x7fffffff;
+    // candidate key = overlap << 16 | (0xffff - j): one warp max reduction
+    // picks the largest overlap, ties to the lowest index; 0 = no candidate
+    uint32_t best = 0u;
     const uint8_t* row = ov + a * blocks;
     for (int m = (a + 1) >> 5; (m << 5) < blocks; ++m) {
       const int j = (m << 5) + lane;
       if (j <= a || j >= blocks || ((mine >> m) & 1u)) continue;
-      const int o = row[j];
-      if (o > best) {
-        best = o;
-        best_j = j;
-      }
+      best = max(best, (static_cast<uint32_t>(row[j]) << 16) | (0xffffu - static_cast<uint32_t>(j)));
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const int ob = __shfl_xor_sync(0xffffffffu, best, off);
-      const int oj = __shfl_xor_sync(0xffffffffu, best_j, off);
-      if (ob > best || (ob == best && oj < best_j)) {
-        best = ob;
-        best_j = oj;
-      }
-    }
-    const int b = best_j == 0x7fffffff ? -1 : best_j;
+    const uint32_t wbest = __reduce_max_sync(0xffffffffu, best);
+    const int b = wbest == 0u ? -1 : static_cast<int>(0xffffu - (wbest & 0xffffu));
     if ((a & 31) == lane) mine |= 1u << (a >> 5);
     if (b >= 0 && (b & 31) == lane) mine |= 1u << (b >> 5);
     if (lane == 0) {
@@ -241,7 +294,8 @@ cudaError_t launch_route(const void* qc, int qc_dtype, const float* kc, int kc_r
   if (blocks > kMaxBlocks) return cudaErrorInvalidValue;
   if (dim != kDim) return cudaErrorInvalidValue;
   const int chunk = blocks < kColChunk ? ((blocks + 15) & ~15) : kColChunk;
-  const size_t smem = sizeof(float) * (kRows * kDim + kDim * (chunk + 1) + kRows * blocks);
+  const bool mma_path = qc_dtype != B2_F32 && kc_round == B2_BF16;
+  const size_t smem = sizeof(float) * ((mma_path ? 0 : kRows * kDim + kDim * (chunk + 1)) + kRows * blocks);
   cudaError_t err = ensure_smem(reinterpret_cast<const void*>(route_kernel), static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   dim3 grid((blocks + kRows - 1) / kRows, batch_heads);
