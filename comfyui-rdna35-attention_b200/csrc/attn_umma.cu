@@ -72,6 +72,8 @@ struct __align__(8) Misc {
   int ntiles;
   int nlist;
   uint32_t sel[2][kMaxSelWords];
+  uint32_t ua[kMaxSelWords];  // selected-block bitsets of the two query blocks (list building)
+  uint32_t ub[kMaxSelWords];
   uint16_t list[kMaxList];
 };
 
@@ -265,39 +267,66 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     mbar_init(&m.c_full, 1);
     mbar_init(&m.mma_done, 1);
     mbar_init(&m.pv_all, 1);
-    int nlist = 0;
-    if (a.mode == 1) {
-      const int32_t* la = a.indices + (int64_t(bh) * a.nqb + qa) * a.nsel;
-      const int32_t* lb = a.indices + (int64_t(bh) * a.nqb + (has_b ? qb : qa)) * a.nsel;
-      const int nbk = (a.tk + 63) / 64;
-      int ia = 0, ib = has_b ? 0 : a.nsel;
-      while ((ia < a.nsel || ib < a.nsel) && nlist < kMaxList) {
-        const int va = ia < a.nsel ? min(max(la[ia], 0), nbk - 1) : 0x7fffffff;
-        const int vb = ib < a.nsel ? min(max(lb[ib], 0), nbk - 1) : 0x7fffffff;
-        uint32_t e;
-        if (va == vb) {
-          e = va | (3u << 14);
-          ++ia;
-          ++ib;
-        } else if (va < vb) {
-          e = va | (1u << 14);
-          ++ia;
-        } else {
-          e = vb | (2u << 14);
-          ++ib;
-        }
-        m.list[nlist++] = static_cast<uint16_t>(e);
+    if (a.mode != 1) {
+      int nlist = 0;
+      if (a.mode == 2) {
+        m.list[nlist++] = static_cast<uint16_t>(qa | (1u << 14));
+        if (has_b) m.list[nlist++] = static_cast<uint16_t>(qb | (2u << 14));
+      } else {
+        nlist = (a.tk + 63) / 64;
       }
-    } else if (a.mode == 2) {
-      m.list[nlist++] = static_cast<uint16_t>(qa | (1u << 14));
-      if (has_b) m.list[nlist++] = static_cast<uint16_t>(qb | (2u << 14));
-    } else {
-      nlist = (a.tk + 63) / 64;
+      m.nlist = nlist;
+      m.ntiles = ntail + nlist;
     }
-    m.nlist = nlist;
-    m.ntiles = ntail + nlist;
     fence_barrier_init();
     fence_proxy_async_smem();
+  }
+  if (a.mode == 1 && warp == 0) {
+    // union of the two query blocks' selected key blocks, sorted, each entry
+    // tagged with the half(s) that selected it: the lanes OR the (clamped)
+    // indices into two bitsets in parallel, then lane l emits the set bits of
+    // word l at the offset given by a warp prefix sum of the popcounts
+    const int nbk = (a.tk + 63) / 64;
+    const int wk = (nbk + 31) >> 5;
+    if (lane < wk) {
+      m.ua[lane] = 0u;
+      m.ub[lane] = 0u;
+    }
+    __syncwarp();
+    const int32_t* la = a.indices + (int64_t(bh) * a.nqb + qa) * a.nsel;
+    const int32_t* lb = a.indices + (int64_t(bh) * a.nqb + (has_b ? qb : qa)) * a.nsel;
+    for (int e = lane; e < a.nsel; e += 32) {
+      const int va = min(max(la[e], 0), nbk - 1);
+      atomicOr(&m.ua[va >> 5], 1u << (va & 31));
+      if (has_b) {
+        const int vb = min(max(lb[e], 0), nbk - 1);
+        atomicOr(&m.ub[vb >> 5], 1u << (vb & 31));
+      }
+    }
+    __syncwarp();
+    const uint32_t wa = lane < wk ? m.ua[lane] : 0u;
+    const uint32_t wb = lane < wk ? m.ub[lane] : 0u;
+    uint32_t u = wa | wb;
+    const int cnt = __popc(u);
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    int pos = incl - cnt;
+    while (u != 0u) {
+      const int bit = __ffs(u) - 1;
+      u &= u - 1u;
+      const uint32_t tag = ((wa >> bit) & 1u) | (((wb >> bit) & 1u) << 1);
+      if (pos < kMaxList) m.list[pos] = static_cast<uint16_t>((lane * 32 + bit) | (tag << 14));
+      ++pos;
+    }
+    const int nlist = min(__shfl_sync(0xffffffffu, incl, 31), kMaxList);
+    if (lane == 0) {
+      m.nlist = nlist;
+      m.ntiles = ntail + nlist;
+    }
   }
   if (ntail > 0) {
     for (int i = threadIdx.x; i < 2 * words; i += kThreads) {
@@ -762,7 +791,7 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   a.nsel = p.nsel;
   a.sel_bits = p.sel_bits;
   a.nb = p.nb;
-  if (p.mode == 1 && 2 * p.nsel > kMaxList) return cudaSuccess;
+  if (p.mode == 1 && (2 * p.nsel > kMaxList || (kv.tokens + 63) / 64 > 32 * kMaxSelWords)) return cudaSuccess;
   if (p.nb > 32 * kMaxSelWords) return cudaSuccess;
   a.has_corr = p.h != nullptr ? 1 : 0;
   a.scale_log2 = p.scale * 1.4426950408889634f;
