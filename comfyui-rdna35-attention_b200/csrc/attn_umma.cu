@@ -13,11 +13,12 @@
 //   * fixed block (mode DIAG): each query block's own key block
 //     (triton_kernel.py:53-100, optional causal mask).
 //
-// Warp roles (352 threads, one CTA per SM):
+// Warp roles (384 threads, one CTA per SM):
 //   warp 0    TMA producer: Q pair once, then K (or centroid) tiles into a
 //             6-stage ring, finally H (first-order operand) for the correction
 //   warp 10   TMA producer of the V tiles (own 6-stage ring)
-//   warp 1    TMEM owner (512 columns) + single-thread MMA issuer:
+//   warps 1 / 11  single-thread MMA issuers, one per softmax warpgroup (warp 1
+//             also owns the 512 TMEM columns):
 //             S(j) = Q K(j)^T  -> TMEM S buffer of warpgroup j%2 (128 x 64 FP32,
 //                                 two buffers per warpgroup)
 //             O   += P(j) V(j) -> TMEM O of warpgroup j%2 (128 x 128 FP32),
@@ -25,7 +26,8 @@
 //             C    = Q H       -> TMEM (reuses warpgroup 0's S columns)
 //             S(j) reuses the buffer of P(j-4), so it is issued only after
 //             that P.V has completed; otherwise S and P.V go out as their
-//             operands arrive.
+//             operands arrive.  Separate issuers keep one warpgroup's chain
+//             from waiting behind the other's.
 //   warps 2-5 / 6-9  two softmax warpgroups taking alternate key tiles (split
 //             K inside the CTA): thread r owns query row r (TMEM lane r);
 //             reads its 64 logits with one tcgen05.ld pair, computes exp2 of
@@ -48,7 +50,7 @@ namespace {
 
 using namespace umma;
 
-constexpr int kThreads = 352;  // K producer, MMA, 2 softmax warpgroups, V producer
+constexpr int kThreads = 384;  // K producer, 2 MMA issuers, 2 softmax warpgroups, V producer
 constexpr int kStages = 6;
 constexpr int kMaxList = 192;  // union of two selected lists
 constexpr int kMaxSelWords = 32;
@@ -66,7 +68,7 @@ struct __align__(8) Misc {
   uint64_t pv_done[2][2];  // [warpgroup][S buffer]
   uint64_t pv_all;         // every P.V complete (before C reuses warpgroup 0's S columns)
   uint64_t c_full;
-  uint64_t mma_done;
+  uint64_t mma_done[2];
   uint32_t tmem;
   int abort_flag;
   int ntiles;
@@ -265,7 +267,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       mbar_init(&m.pv_done[w][1], 1);
     }
     mbar_init(&m.c_full, 1);
-    mbar_init(&m.mma_done, 1);
+    mbar_init(&m.mma_done[0], 1);
+    mbar_init(&m.mma_done[1], 1);
     mbar_init(&m.pv_all, 1);
     if (a.mode != 1) {
       int nlist = 0;
@@ -392,33 +395,37 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 11) {
+    // ------------------------------------------------------------ MMA issuers
+    // One issuing thread per softmax warpgroup (tcgen05.commit tracks the
+    // issuing thread's MMAs), so the two warpgroups' S -> P -> P.V chains
+    // never wait behind each other.  Warpgroup w owns key tiles j = w, w+2, ...
+    // (local index i = j / 2) and S buffers i % 2.
     if (elect_one()) {
+      const int w = warp == 1 ? 0 : 1;
       const uint32_t q_addr = smem_u32(q_s);
-      // S(j) may go out once the P.V of tile j-4 (same S buffer) has completed
-      // and its K tile is in; P.V(j) once P(j) and V(j) are.  Each warpgroup
-      // has two S buffers, so S(j+2) is ready before it finishes the softmax
-      // of tile j.  Whichever is ready first is issued, S preferred.
+      const int cnt = (n - w + 1) >> 1;
+      // S(i) may go out once P.V(i-2) (same S buffer) has completed and its K
+      // tile is in; P.V(i) once P(i) and V(i) are.  S is preferred.
       bool ok = mbar_wait(&m.q_full, 0, abort_flag, a.status, 3);
       int ns = 0, npv = 0;
       const long long start = clock64();
-      while (ok && npv < n) {
+      while (ok && npv < cnt) {
         bool did = false;
-        if (ns < n) {
-          const int w = ns & 1, i = ns >> 1;
-          const bool buf_free = ns < 4 || (ns - 4 < npv && mbar_test_wait(&m.pv_done[w][i & 1], ((i - 2) >> 1) & 1));
-          if (buf_free && mbar_test_wait(&m.k_full[ns % kStages], (ns / kStages) & 1)) {
-            ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, ns, trace);
+        if (ns < cnt) {
+          const int j = 2 * ns + w;
+          const bool buf_free = ns < 2 || (ns - 2 < npv && mbar_test_wait(&m.pv_done[w][ns & 1], ((ns - 2) >> 1) & 1));
+          if (buf_free && mbar_test_wait(&m.k_full[j % kStages], (j / kStages) & 1)) {
+            ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, j, trace);
             ++ns;
             did = true;
           }
         }
         if (!did && ok && npv < ns) {
-          const int w = npv & 1, i = npv >> 1;
-          if (mbar_test_wait(&m.p_full[w][i & 1], (i >> 1) & 1) &&
-              mbar_test_wait(&m.v_full[npv % kStages], (npv / kStages) & 1)) {
-            ok = issue_pv<BF16>(m, smem, tmem, a, abort_flag, npv);
+          const int j = 2 * npv + w;
+          if (mbar_test_wait(&m.p_full[w][npv & 1], (npv >> 1) & 1) &&
+              mbar_test_wait(&m.v_full[j % kStages], (j / kStages) & 1)) {
+            ok = issue_pv<BF16>(m, smem, tmem, a, abort_flag, j);
             ++npv;
             did = true;
           }
@@ -434,12 +441,12 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           }
         }
       }
-      if (ok && a.has_corr) {
-        // C overwrites warpgroup 0's S columns: every P.V must have read its P
+      if (w == 0 && ok && a.has_corr) {
+        // C overwrites warpgroup 0's S columns: its P.V must have read its P
         mma_commit(&m.pv_all);
         ok = mbar_wait(&m.pv_all, 0, abort_flag, a.status, 24);
       }
-      if (ok && a.has_corr) {
+      if (w == 0 && ok && a.has_corr) {
         // C = Q H as two N=64 products, one per 64-column half of H
         const uint32_t idesc_c = idesc_f16(128, 64, BF16, false, true);
         for (int hh = 0; ok && hh < 2; ++hh) {
@@ -460,11 +467,11 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       }
       // every MMA this thread issued completes before TMEM is released
       // (bounded by time only, even after an abort)
-      mma_commit(&m.mma_done);
+      mma_commit(&m.mma_done[w]);
       int no_abort = 0;
-      mbar_wait(&m.mma_done, 0, &no_abort, a.status, 7);
+      mbar_wait(&m.mma_done[w], 0, &no_abort, a.status, 7);
     }
-  } else {
+  } else if (warp >= 2 && warp <= 9) {
     // ------------------------------------------------------------ softmax
     const int wg = (warp - 2) >> 2;   // 0 or 1
     const int sub = warp & 3;         // TMEM sub-partition of this warp
