@@ -17,7 +17,9 @@ namespace b2 {
 namespace {
 
 constexpr int kRows = 16;       // query blocks per CTA
-constexpr int kThreadsR = 256;  // 16 rows x 16 column lanes
+constexpr int kThreadsR = 512;  // 16 warps: one query-block row each for the top-k
+constexpr int kRowsPerWarp = kRows / (kThreadsR / 32);
+constexpr int kFmaThreads = 256;  // FP32 path: 16 rows x 16 column lanes
 constexpr int kColChunk = 256;  // key centroids staged per pass
 constexpr int kDim = 128;
 constexpr int kMaxBlocks = 1024;
@@ -143,6 +145,7 @@ route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict
       }
       __syncthreads();
       const int na = (ncol + 15) >> 4;  // accumulators in use (<= 16)
+      if (t < kFmaThreads) {
       float acc[kColChunk / 16];
   #pragma unroll
       for (int i = 0; i < kColChunk / 16; ++i) acc[i] = 0.f;
@@ -164,13 +167,14 @@ route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict
           scores[r * blocks + c0 + j] = sc;
         }
       }
+      }
     }
   }
   __syncthreads();
-  // ---- per-row top-k: warp w handles rows 2w and 2w+1
+  // ---- per-row top-k: warp w handles rows kRowsPerWarp*w ...
   const int warp = t >> 5;
   const int lane = t & 31;
-  for (int rr = 2 * warp; rr < 2 * warp + 2; ++rr) {
+  for (int rr = kRowsPerWarp * warp; rr < kRowsPerWarp * (warp + 1); ++rr) {
     const int qi = row0 + rr;
     if (qi >= blocks) break;
     float* srow = scores + rr * blocks;
@@ -258,10 +262,21 @@ __global__ void __launch_bounds__(256) pair_kernel(const uint32_t* __restrict__ 
     // picks the largest overlap, ties to the lowest index; 0 = no candidate
     uint32_t best = 0u;
     const uint8_t* row = ov + a * blocks;
-    for (int m = (a + 1) >> 5; (m << 5) < blocks; ++m) {
-      const int j = (m << 5) + lane;
-      if (j <= a || j >= blocks || ((mine >> m) & 1u)) continue;
-      best = max(best, (static_cast<uint32_t>(row[j]) << 16) | (0xffffu - static_cast<uint32_t>(j)));
+    if (words <= 8) {
+      // fixed trip count: the byte loads of all candidate words go out together
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int j = (m << 5) + lane;
+        const bool cand = m < words && j > a && j < blocks && !((mine >> m) & 1u);
+        const uint32_t o = cand ? row[j] : 0u;
+        if (cand) best = max(best, (o << 16) | (0xffffu - static_cast<uint32_t>(j)));
+      }
+    } else {
+      for (int m = (a + 1) >> 5; (m << 5) < blocks; ++m) {
+        const int j = (m << 5) + lane;
+        if (j <= a || j >= blocks || ((mine >> m) & 1u)) continue;
+        best = max(best, (static_cast<uint32_t>(row[j]) << 16) | (0xffffu - static_cast<uint32_t>(j)));
+      }
     }
     const uint32_t wbest = __reduce_max_sync(0xffffffffu, best);
     const int b = wbest == 0u ? -1 : static_cast<int>(0xffffu - (wbest & 0xffffu));
