@@ -34,6 +34,10 @@ namespace {
 using namespace umma;
 
 constexpr int kThreads = 320;
+#ifndef B2_SUM_UNROLL
+#define B2_SUM_UNROLL 8
+#endif
+constexpr int kSumUnroll = B2_SUM_UNROLL;  // 8-row groups of the column sums unrolled together
 constexpr int kStages = 3;
 constexpr uint32_t kTile = 64 * 128 * 2;  // one 64-row x 128-col 16-bit tile (two 8 KB halves)
 constexpr uint32_t kStageBytes = 3 * kTile;
@@ -58,13 +62,6 @@ struct Layout {
   static constexpr uint32_t total = misc + sizeof(Misc);
 };
 static_assert(Layout::total <= 232448, "shared memory budget");
-
-// byte offset of element (row r, column c) in a 128-byte-swizzled 64x128 tile
-__device__ __forceinline__ uint32_t sw_off(int r, int c) {
-  const int half = c >> 6;
-  const int cc = c & 63;
-  return half * 8192 + r * 128 + ((((cc >> 3) ^ (r & 7))) << 4) + ((cc & 7) << 1);
-}
 
 struct StatsArgs {
   int kind;  // 0 linear 4D map, 1 tiled 5D map
@@ -276,7 +273,7 @@ stats_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_consta
           const char* base = tile + (col >> 6) * 8192 + ((col & 7) << 1);
           const int chunk = (col & 63) >> 3;
           const int full_rows = len & ~7;
-#pragma unroll 1
+#pragma unroll kSumUnroll
           for (int rr = 0; rr < full_rows; rr += 8) {
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
