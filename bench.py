@@ -71,6 +71,24 @@ def _dist():
     return world, rank, local
 
 
+def max_over_ranks(x: float, device) -> float:
+    """The slowest rank's time: all-reduce MAX over the process group (NCCL
+    on the GPUs, gloo in the CPU tests); the value itself with one rank."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_value(world: int, ms: float) -> float:
+    """Whole-job dense-equivalent TFLOP/s: every rank runs one full call
+    (weak scaling), the job takes the slowest rank's time."""
+    return world * DENSE_FLOP / (ms * 1e-3) / 1e12
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -210,13 +228,8 @@ def run_b200(args) -> None:
         ms = _timed(step, args.steps, stream)
         barrier()
     clock_info = clocks.summary()
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
-    value = world * DENSE_FLOP / (ms * 1e-3) / 1e12
+    ms = max_over_ranks(ms, device)
+    value = job_value(world, ms)
 
     # ---- end to end through the public API: pinned host q/k/v -> device,
     # call, output -> pinned host, all inside the timed region
@@ -234,12 +247,7 @@ def run_b200(args) -> None:
     barrier()
     e2e_ms = _timed(e2e_step, max(2, args.steps // 2), stream)
     barrier()
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
+    e2e_ms = max_over_ranks(e2e_ms, device)
     h2d = sum(h.numel() * h.element_size() for h in host)
     d2h = out_host.numel() * out_host.element_size()
 
@@ -268,7 +276,7 @@ def run_b200(args) -> None:
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) + per-tile N(0,0.5) offsets)",
             "config": CONFIG, "clocks": clock_info,
-            "e2e": {"value": round(world * DENSE_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT,
+            "e2e": {"value": round(job_value(world, e2e_ms), 2), "unit": UNIT,
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": 6 * args.steps,
             "roofline": roofline,

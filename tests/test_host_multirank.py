@@ -1,0 +1,71 @@
+"""Multi-process host logic of bench.py on CPU: two gloo ranks.
+
+bench.py runs one process per GPU (weak scaling, no collective on the data
+path); the only cross-rank steps are the max over ranks of the timed
+region and rank-0-only output.  Those run here with the gloo backend on
+127.0.0.1, without a GPU.
+"""
+import io
+import os
+import pathlib
+import socket
+import sys
+from contextlib import redirect_stdout
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w, r, local = bench._dist()
+        ms = 1.0 + rank  # rank 1 is the slow one
+        slowest = bench.max_over_ranks(ms, torch.device("cpu"))
+        value = bench.job_value(w, slowest)
+        # the reference arm runs on rank 0 only; other ranks print nothing
+        buf = io.StringIO()
+        if rank != 0:
+            args = type("A", (), {"cpu_heads": 1, "warmup": 0, "steps": 0})()
+            with redirect_stdout(buf):
+                bench.run_reference(args)
+        results[rank] = (w, r, local, slowest, value, buf.getvalue())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_take_the_slowest_time():
+    world = 2
+    results = mp.get_context("spawn").Manager().dict()
+    mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    for rank in range(world):
+        w, r, local, slowest, value, out = results[rank]
+        assert (w, r, local) == (world, rank, rank)
+        assert slowest == 2.0  # max over ranks, seen identically by every rank
+        assert abs(value - world * bench.DENSE_FLOP / 2e-3 / 1e12) < 1e-9
+        assert out == ""
+
+
+def test_single_process_needs_no_group():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    assert bench.max_over_ranks(3.5, torch.device("cpu")) == 3.5
+    assert abs(bench.job_value(1, 1.0) - bench.DENSE_FLOP / 1e-3 / 1e12) < 1e-9
