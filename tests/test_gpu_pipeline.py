@@ -70,3 +70,49 @@ def test_dense_large_logits_match_sdpa(pisa):
     got = _repeat(lambda: pisa.full_attention(qd, kd, vd, 128 ** -0.5)).float()
     exp = F.scaled_dot_product_attention(qd.float(), kd.float(), vd.float(), scale=128 ** -0.5)
     torch.testing.assert_close(got, exp, atol=2e-2, rtol=2e-2)
+
+
+def _greedy_pairs(sel):
+    """Restatement of pair_kernel: blocks in ascending order; each unpaired
+    block takes the later unpaired block of largest selection overlap (ties:
+    lowest index), or stays single when none is left."""
+    nb = sel.shape[0]
+    ov = (sel[:, None, :] & sel[None, :, :]).sum(-1)
+    used = [False] * nb
+    pairs = []
+    for a in range(nb):
+        if used[a]:
+            continue
+        used[a] = True
+        cands = [(int(ov[a, j]), -j) for j in range(a + 1, nb) if not used[j]]
+        b = -max(cands)[1] if cands else -1
+        if b >= 0:
+            used[b] = True
+        pairs.append((a, b))
+    return pairs
+
+
+@pytest.mark.parametrize("blocks", [7, 144, 300])
+def test_pairing_kernel_matches_restatement(pisa, blocks):
+    import ctypes
+
+    from b200_pisa import LIB, check
+
+    gen = torch.Generator().manual_seed(blocks)
+    bh, words = 3, (blocks + 31) // 32
+    sel = torch.rand((bh, blocks, blocks), generator=gen) < 0.2
+    packed = torch.zeros((bh, blocks, words), dtype=torch.int64)
+    for w in range(words):
+        chunk = sel[:, :, 32 * w: 32 * w + 32].to(torch.int64)
+        packed[:, :, w] = (chunk << torch.arange(chunk.shape[-1], dtype=torch.int64)).sum(-1)
+    packed = packed.to(torch.int32).to(DEV)  # two's complement bit pattern of the uint32 words
+    npairs = (blocks + 1) // 2
+    out = torch.full((bh, npairs, 2), -7, dtype=torch.int32, device=DEV)
+    check(LIB.b2_pisa_pair(ctypes.c_void_p(packed.data_ptr()), bh, blocks, ctypes.c_void_p(out.data_ptr()),
+                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    got = out.cpu()
+    for b in range(bh):
+        exp = _greedy_pairs(sel[b].numpy())
+        assert [tuple(p) for p in got[b].tolist()] == exp
+        seen = sorted(x for p in exp for x in p if x >= 0)
+        assert seen == list(range(blocks))
