@@ -116,3 +116,13 @@ def test_pairing_kernel_matches_restatement(pisa, blocks):
         assert [tuple(p) for p in got[b].tolist()] == exp
         seen = sorted(x for p in exp for x in p if x >= 0)
         assert seen == list(range(blocks))
+
+
+def test_spatial_batch_two_matches_oracle(pisa):
+    # the benchmark's batch of 2: the 8x8-tiled maps address frame * batch
+    q, k, v = oracle.anima_inputs(batch=2, heads=2, seed=13)
+    qd, kd, vd = (to_dev_bhtd(x) for x in (q, k, v))
+    got = _repeat(lambda: pisa.forward_spatial_bhtd(qd, kd, vd, exact_blocks=23)).cpu().float()
+    exp, _ = oracle.hyd_forward_spatial(q, k, v, 23)
+    assert got.shape == (2, 9216, 256)
+    torch.testing.assert_close(got, exp.float(), **TOL)
