@@ -15,6 +15,12 @@ ranks.  The inputs (226 MB of q/k/v) exceed the 126 MB L2, so no extra flush.
 ``--impl reference`` times the reference's PyTorch HYD path restated on the
 host CPU (oracle/pisa_oracle.py) on a bounded sample and reports the same
 metric.
+
+``--workload`` selects one of the other configs instead of the headline one
+(full_self / full_cross: config 2; minimax_h3_t9170 / minimax_h3_t16500:
+config 4; generic_pisa_video: config 5; fixed_block_fp32: config 1).  Each
+prints the same JSON line for its own public call, with the roofline of its
+dominant kernel and a bounded CPU sample of the oracle.
 """
 from __future__ import annotations
 
@@ -402,6 +408,431 @@ def run_reference(args) -> None:
     }))
 
 
+# ---------------------------------------------------------- other configs
+# The other BASELINE.json configs, each timed through its public call under
+# the same JSON contract (``--workload``).  Config 3 ("anima") stays the
+# headline line; these are reported beside it.
+
+
+def _randn(shape, gen, dtype=torch.bfloat16):
+    return torch.randn(shape, generator=gen).to(dtype)
+
+
+class Workload:
+    """One secondary config: host inputs, the public call on device views,
+    the roofline of its dominant kernel, and a bounded CPU sample."""
+
+    def __init__(self, name, config, metric, unit, value_work, roof_bound, roof_work, launches, flush=False):
+        self.name, self.config, self.metric, self.unit = name, config, metric, unit
+        self.value_work, self.roof_bound, self.roof_work = value_work, roof_bound, roof_work
+        self.launches, self.flush = launches, flush
+        self.value_scale = 1e9 if unit.startswith("GFLOP") else 1e12
+
+    # subclasses: host_inputs(seed) -> list of CPU tensors; views(dev) -> call
+    # arguments; call(api, *args) -> output; kernel(api, *args) -> a callable
+    # timing the dominant kernel alone; cpu_call() -> (seconds per full call,
+    # sample text)
+
+
+class FullWorkload(Workload):
+    """Config 2: exact full attention, self (Tk=9216) or cross (Tk=512)."""
+
+    def __init__(self, tk):
+        flop = 4.0 * B * H * T * tk * D
+        name = "full_self" if tk == T else "full_cross"
+        super().__init__(name, {"workload": name, "batch": B, "heads": H, "q_tokens": T, "kv_tokens": tk,
+                                "head_dim": D, "layout": "contiguous [B,H,T,D]",
+                                "l2": "q/out 151 MB > 126 MB L2 (no flush)"},
+                         f"full attention call ms & TFLOP/s, B=2 H=16 Tq=9216 Tk={tk} D=128 bf16", "TFLOP/s",
+                         flop, "tensor", flop, 1)
+        self.tk = tk
+
+    def host_inputs(self, seed):
+        gen = torch.Generator().manual_seed(seed)
+        return [_randn((B, H, T, D), gen), _randn((B, H, self.tk, D), gen), _randn((B, H, self.tk, D), gen)]
+
+    def views(self, dev):
+        return dev
+
+    def call(self, api, q, k, v):
+        return api.full_attention(q, k, v, D ** -0.5)
+
+    def cpu_call(self):
+        import pisa_oracle
+
+        if not hasattr(self, "_cpu"):
+            self._cpu = self.host_inputs(0)
+        q, k, v = self._cpu
+        t0 = time.perf_counter()
+        pisa_oracle.full_attention(q[0, :1], k[0, :1], v[0, :1])
+        return (time.perf_counter() - t0) * B * H, f"1 of {B * H} (batch, head) pairs, scaled x{B * H}"
+
+
+class H3Workload(Workload):
+    """Config 4: MiniMax-H3 exact attention from the interleaved projection
+    [1,T,3,56,128]; q/k are strided views, v a contiguous clone viewed BHTD
+    (bench_minimax_h3_gfx1151_attention.py:90-94).  One call = the override's
+    native path (attention straight from the views + merged [B,T,H*D] output;
+    no pack copy is needed)."""
+
+    HEADS = 56
+
+    def __init__(self, tokens):
+        flop = 4.0 * self.HEADS * tokens * tokens * D
+        name = f"minimax_h3_t{tokens}"
+        super().__init__(name, {"workload": name, "batch": 1, "heads": self.HEADS, "tokens": tokens, "head_dim": D,
+                                "layout": "q,k strided views of qkv [1,T,3,56,128]; v contiguous; out [1,T,56*128]",
+                                "l2": "inputs > 126 MB L2 (no flush)"},
+                         f"MiniMax-H3 attention call ms & TFLOP/s, H=56 T={tokens} D=128 bf16", "TFLOP/s",
+                         flop, "tensor", flop, 1)
+        self.tokens = tokens
+
+    def host_inputs(self, seed):
+        gen = torch.Generator().manual_seed(self.tokens if seed == 0 else self.tokens + seed)
+        qkv = _randn((1, self.tokens, 3, self.HEADS, D), gen)
+        return [qkv, qkv[:, :, 2].contiguous()]
+
+    def views(self, dev):
+        qkv, v = dev
+        return qkv[:, :, 0].permute(0, 2, 1, 3), qkv[:, :, 1].permute(0, 2, 1, 3), v.permute(0, 2, 1, 3)
+
+    def call(self, api, q, k, v):
+        from rdna35_block_attention.minimax_h3_gfx1151_attention import minimax_h3_attention
+
+        return minimax_h3_attention(q, k, v)
+
+    def cpu_call(self):
+        import pisa_oracle
+
+        if not hasattr(self, "_cpu"):
+            self._cpu = self.host_inputs(0)
+        qkv, v = self._cpu
+        q, k = qkv[:, :, 0, :1].permute(0, 2, 1, 3), qkv[:, :, 1, :1].permute(0, 2, 1, 3)
+        t0 = time.perf_counter()
+        pq, pk, pv, _ = pisa_oracle.h3_pack(q, k, v[:, :, :1].permute(0, 2, 1, 3))
+        pisa_oracle.full_attention(pq, pk, pv)
+        return (time.perf_counter() - t0) * self.HEADS, f"1 of {self.HEADS} heads (pack + attention), scaled x56"
+
+
+class GenericWorkload(Workload):
+    """Config 5: generic PISA video self-attention [1,40,32760,128], 512
+    blocks (last 56 tokens), ceil(512/6) = 86 exact, first-order on."""
+
+    HEADS, TOKENS = 40, 32760
+
+    def __init__(self):
+        nb = (self.TOKENS + 63) // 64
+        self.nb, self.exact = nb, math.ceil(nb / 6)
+        exact = 4.0 * self.HEADS * self.TOKENS * 64 * self.exact * D  # every row x 86 selected 64-key blocks
+        tail = 4.0 * self.HEADS * self.TOKENS * nb * D
+        corr = 2.0 * self.HEADS * self.TOKENS * D * D
+        dense = 4.0 * self.HEADS * self.TOKENS * self.TOKENS * D
+        super().__init__("generic_pisa_video", {"workload": "generic_pisa_video", "batch": 1, "heads": self.HEADS,
+                                                "tokens": self.TOKENS, "head_dim": D, "blocks": nb,
+                                                "exact_blocks": self.exact, "layout": "block-major [1,40,T,128]",
+                                                "l2": "inputs 1.0 GB > 126 MB L2 (no flush)"},
+                         "generic PISA call ms & dense-equiv TFLOP/s, H=40 T=32760 D=128 bf16, 86/512 exact",
+                         "dense-equiv TFLOP/s", dense, "tensor", exact + tail + corr, 5)
+
+    def host_inputs(self, seed):
+        import pisa_oracle
+
+        q, k, v = pisa_oracle.generic_inputs(self.HEADS, self.TOKENS, seed)
+        return [x.unsqueeze(0) for x in (q, k, v)]
+
+    def _cpu_inputs(self):
+        if not hasattr(self, "_cpu"):
+            import pisa_oracle
+
+            self._cpu = pisa_oracle.generic_inputs(1, self.TOKENS, 0)
+        return self._cpu
+
+    def views(self, dev):
+        return dev
+
+    def call(self, api, q, k, v):
+        return api.generic_forward(q, k, v, self.exact, D ** -0.5)
+
+    def kernel(self, api, q, k, v):
+        """The fused attention launch alone, fed by this call's own statistics,
+        routing and pairing (C-ABI entry points); the other stages are
+        returned beside it for their own timings."""
+        import ctypes
+
+        from b200_pisa import LIB, _lib, check
+
+        bh, nb, dev = self.HEADS, self.nb, q.device
+        stream = lambda: torch.cuda.current_stream(dev).cuda_stream  # noqa: E731
+        qv, kv, vv = (_lib.view(x) for x in (q, k, v))
+        qc = torch.empty((bh, nb, D), device=dev, dtype=torch.float32)
+        kc = torch.empty_like(qc)
+        vsum = torch.empty_like(qc)
+        hsum = torch.empty((bh, D, D), device=dev, dtype=torch.float32)
+        ws = torch.empty(int(LIB.b2_stats_workspace_bytes(bh, self.TOKENS, D)), device=dev, dtype=torch.uint8)
+        idx = torch.empty((bh, nb, self.exact), device=dev, dtype=torch.int32)
+        sel = torch.empty((bh, nb, (nb + 31) // 32), device=dev, dtype=torch.int32)
+        pairs = torch.empty((bh, (nb + 1) // 2, 2), device=dev, dtype=torch.int32)
+
+        def stats():
+            check(LIB.b2_pisa_block_stats(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), _lib.STATS_GENERIC,
+                                          qc.data_ptr(), kc.data_ptr(), vsum.data_ptr(), hsum.data_ptr(), None, None,
+                                          ws.data_ptr(), stream()))
+
+        def route():
+            check(LIB.b2_pisa_route(qc.data_ptr(), _lib.B2_F32, kc.data_ptr(), _lib.B2_F32, None, bh, nb, D,
+                                    self.exact, D ** -0.5, -2, idx.data_ptr(), sel.data_ptr(), stream()))
+
+        def pair():
+            check(LIB.b2_pisa_pair(sel.data_ptr(), bh, nb, pairs.data_ptr(), stream()))
+
+        stats()
+        route()
+        pair()
+        lens = torch.full((nb,), 64.0, device=dev)
+        lens[-1] = self.TOKENS - 64 * (nb - 1)
+        kc16 = kc.to(torch.bfloat16)
+        vc16 = (vsum / lens[None, :, None]).to(torch.bfloat16)
+        h16 = hsum.to(torch.bfloat16)
+        out = torch.empty_like(q)
+        ov = _lib.view(out)
+
+        def attn():
+            check(LIB.b2_pisa_attention(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(ov),
+                                        idx.data_ptr(), self.exact, sel.data_ptr(), pairs.data_ptr(), kc16.data_ptr(),
+                                        vc16.data_ptr(), h16.data_ptr(), D ** -0.5, None, stream()))
+
+        # the views hold raw pointers: the tensors behind them must outlive
+        # every launch (CUDA-graph capture empties the allocator's cache)
+        attn.keep_alive = (q, k, v, out, qc, kc, vsum, hsum, ws, idx, sel, pairs, kc16, vc16, h16)
+        attn.components = {"stats_ms": stats, "route_ms": route, "pair_ms": pair}
+        return attn
+
+    def cpu_call(self):
+        import pisa_oracle
+
+        q, k, v = self._cpu_inputs()
+        t0 = time.perf_counter()
+        pisa_oracle.generic_forward(q, k, v, self.exact)
+        return (time.perf_counter() - t0) * self.HEADS, f"1 of {self.HEADS} heads at T=32760, scaled x40"
+
+
+class FixedWorkload(Workload):
+    """Config 1: fixed 64-token block-diagonal attention, FP32 [1,8,1024,64]."""
+
+    def __init__(self):
+        self.shape = (1, 8, 1024, 64)
+        flop = 4.0 * 8 * 1024 * 64 * 64
+        nbytes = 4.0 * 4 * 8 * 1024 * 64
+        super().__init__("fixed_block_fp32", {"workload": "fixed_block_fp32", "batch": 1, "heads": 8, "tokens": 1024,
+                                              "head_dim": 64, "block": 64,
+                                              "l2": "8.4 MB inputs: L2 flushed (256 MB write) before every step"},
+                         "fixed-block attention call ms & GFLOP/s, B=1 H=8 T=1024 D=64 fp32", "GFLOP/s",
+                         flop, "hbm", nbytes, 1, flush=True)
+
+    def host_inputs(self, seed):
+        gens = [torch.Generator().manual_seed(s) for s in (0 + 3 * seed, 1 + 3 * seed, 2 + 3 * seed)]
+        return [torch.randn(self.shape, generator=g) for g in gens]
+
+    def views(self, dev):
+        return dev
+
+    def call(self, api, q, k, v):
+        from rdna35_block_attention.dispatch import fixed_block_attention
+
+        return fixed_block_attention(q, k, v, mode="b200")
+
+    def kernel(self, api, q, k, v):
+        """The FP32 block-diagonal launch alone through its C-ABI entry."""
+        import ctypes
+
+        from b200_pisa import LIB, _lib, check
+
+        out = torch.empty_like(q)
+        qv, kv, vv, ov = (_lib.view(x) for x in (q, k, v, out))
+
+        def fixed():
+            check(LIB.b2_fixed_block_attention(ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv),
+                                               ctypes.byref(ov), ctypes.c_float(0.125), 0,
+                                               ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)))
+
+        fixed.keep_alive = (q, k, v, out)
+        return fixed
+
+    def cpu_call(self):
+        import pisa_oracle
+
+        q, k, v = self.host_inputs(0)
+        reps = 50
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            pisa_oracle.fixed_block_attention(q, k, v)
+        return (time.perf_counter() - t0) / reps, f"the whole config, mean of {reps} calls"
+
+
+WORKLOADS = {
+    "full_self": lambda: FullWorkload(T),
+    "full_cross": lambda: FullWorkload(512),
+    "minimax_h3_t9170": lambda: H3Workload(9170),
+    "minimax_h3_t16500": lambda: H3Workload(16500),
+    "generic_pisa_video": GenericWorkload,
+    "fixed_block_fp32": FixedWorkload,
+}
+
+
+def _timed_flushed(fn, steps, stream, flush):
+    """Mean device time of `fn` over `steps` calls, each after a write of a
+    buffer twice the size of L2 (outside the timed events).  A short device
+    sleep after the flush keeps the GPU busy while the host issues the step,
+    so the events bracket device work, not host launch latency."""
+    total = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        torch.cuda._sleep(400_000)  # ~0.2 ms of device time
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        fn()
+        end.record(stream)
+        end.synchronize()
+        total += start.elapsed_time(end)
+    return total / steps
+
+
+def run_workload(args, wl) -> None:
+    world, rank, local = _dist()
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import b200_pisa as api
+
+    api.prepare(local)
+    host = [x.contiguous().pin_memory() for x in wl.host_inputs(rank)]
+    dev = [h.to(device) for h in host]
+    call_args = wl.views(dev)
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device) if wl.flush else None
+
+    def step():
+        return wl.call(api, *call_args)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def timed(fn, steps):
+        return _timed_flushed(fn, steps, stream, flush) if flush is not None else _timed(fn, steps, stream)
+
+    with ClockSampler(local) as clocks:
+        barrier()
+        ms = timed(step, args.steps)
+        barrier()
+    clock_info = clocks.summary()
+    ms = max_over_ranks(ms, device)
+    value = world * wl.value_work / (ms * 1e-3) / wl.value_scale
+
+    # end to end: pinned host inputs -> device, call, output -> pinned host
+    sample_out = step()
+    out_host = torch.empty(sample_out.shape, dtype=sample_out.dtype).pin_memory()
+    dev_e2e = [torch.empty_like(h, device=device) for h in host]
+    e2e_args = wl.views(dev_e2e)
+
+    def e2e_step():
+        for d_, h_ in zip(dev_e2e, host):
+            d_.copy_(h_, non_blocking=True)
+        out_host.copy_(wl.call(api, *e2e_args), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e2e_ms = max_over_ranks(timed(e2e_step, max(2, args.steps // 2)), device)
+    barrier()
+
+    # the dominant kernel alone (graph of back-to-back launches, or flushed)
+    kernel = wl.kernel(api, *call_args) if hasattr(wl, "kernel") else step
+    kernel()
+    torch.cuda.synchronize(device)
+    components = {}
+    if flush is not None:
+        kernel_ms = _timed_flushed(kernel, args.steps, stream, flush)
+    else:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            kernel_ms = _graph_timed(kernel, args.steps, side)
+            for name, fn in getattr(kernel, "components", {}).items():
+                components[name] = round(_graph_timed(fn, args.steps, side), 4)
+        torch.cuda.synchronize(device)
+    peaks = _peaks()
+    if wl.roof_bound == "tensor":
+        achieved, peak, unit = wl.roof_work / (kernel_ms * 1e-3) / 1e12, peaks["bf16"], "TFLOP/s"
+    else:
+        achieved, peak, unit = wl.roof_work / (kernel_ms * 1e-3) / 1e9, peaks["hbm"], "GB/s"
+    if rank == 0:
+        line = {
+            "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32" if wl.flush else "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": wl.config, "clocks": clock_info,
+            "e2e": {"value": round(world * wl.value_work / (e2e_ms * 1e-3) / wl.value_scale, 3), "unit": wl.unit,
+                    "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h in host),
+                    "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+            "gpu_launches": wl.launches * args.steps,
+            "roofline": {"bound": wl.roof_bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                         "frac": round(achieved / peak, 4), "peak_source": peaks["source"],
+                         "kernel_ms": round(kernel_ms, 4), "traffic": None,
+                         **({"component_ms": components} if components else {})},
+        }
+        if not args.no_cpu_baseline and world == 1:
+            torch.set_num_threads(os.cpu_count() or 1)
+            sec, sample = wl.cpu_call()
+            line["cpu_baseline"] = {"value": round(wl.value_work / sec / wl.value_scale, 5), "unit": wl.unit,
+                                    "cores": torch.get_num_threads(), "kind": "port", "sample": sample,
+                                    "ms_per_call_extrapolated": round(sec * 1e3, 2)}
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_workload_reference(args, wl) -> None:
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    for _ in range(args.warmup):
+        wl.cpu_call()
+    samples = []
+    for _ in range(args.steps):
+        sec, sample = wl.cpu_call()
+        samples.append(sec)
+    sec = statistics.median(samples)
+    value = wl.value_work / sec / wl.value_scale
+    print(json.dumps({
+        "impl": "reference", "metric": wl.metric, "value": round(value, 5), "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if wl.flush else "bf16", "data": "synthetic",
+        "config": wl.config,
+        "cpu_baseline": {"value": round(value, 5), "unit": wl.unit, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -409,6 +840,8 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--cpu-heads", type=int, default=1)
+    parser.add_argument("--workload", default="anima", choices=["anima", *WORKLOADS],
+                        help="anima = the headline config 3; the others time the remaining configs")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--profile-only", action="store_true",
                         help="run warm-ups and K plain steps only (for ncu launch lists / captures)")
@@ -417,7 +850,10 @@ def main() -> None:
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload != "anima":
+        wl = WORKLOADS[args.workload]()
+        (run_workload_reference if args.impl == "reference" else run_workload)(args, wl)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

@@ -304,7 +304,7 @@ int b2_pisa_route(const void* qc, int32_t qc_dtype, const float* kc, int32_t kc_
 int b2_pisa_pair(const uint32_t* sel_bits, int32_t batch_heads, int32_t blocks, int32_t* pairs, void* stream) {
   if (!sel_bits || !pairs) return fail(B2_ERR_INVALID, "pairing pointers must be non-NULL");
   if (batch_heads <= 0 || blocks <= 0) return fail(B2_ERR_INVALID, "pairing sizes must be positive");
-  if (blocks > 448) return fail(B2_ERR_UNSUPPORTED, "pairing supports at most 448 blocks");
+  if (!pair_supported(blocks)) return fail(B2_ERR_UNSUPPORTED, "pairing supports at most 608 blocks");
   const cudaError_t err = launch_pair(sel_bits, batch_heads, blocks, pairs, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "PISA pairing launch");
   return ok();
@@ -389,7 +389,7 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
     err = cudaMemsetAsync(w.sel, 0, size_t(bh) * nb * words * 4, st);
     if (err != cudaSuccess) return cuda_fail(err, "selection reset");
   }
-  const bool paired = exact_blocks > 0 && nb <= 448;  // overlap matrix must fit in shared memory
+  const bool paired = exact_blocks > 0 && pair_supported(nb);  // overlaps must fit in shared memory
   if (paired) {
     err = launch_pair(w.sel, bh, nb, w.pairs, st);
     if (err != cudaSuccess) return cuda_fail(err, "PISA pairing launch");

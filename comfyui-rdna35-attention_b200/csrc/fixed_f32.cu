@@ -2,54 +2,94 @@
 // semantics of rdna35_block_attention/reference.py:159-200: FP32 scores,
 // optional causal mask, softmax, FP32 P.V).  Tensor cores would round the
 // operands, so this path runs on FP32 FMA units; the work is tiny (64x64xD
-// per block) and bound by reading Q/K/V once.
+// per block) and bound by reading Q/K/V once plus launch latency.
 #include "common.cuh"
 
 namespace b2 {
 namespace {
 
 constexpr int kFThreads = 256;
+constexpr int kFRows = 32;  // query rows per CTA: half of a 64-token block
 
+// One CTA = 32 query rows of one block against the block's 64 keys.  Thread
+// (ty, tx) = (t / 16, t % 16) owns rows ty and ty + 16; its score columns are
+// tx + 16 i (i < 4) and its output columns tx + 16 i (i < D / 16), so the
+// shared-memory reads of K^T, P and V are conflict-free or broadcasts.
+// Dot products and P.V sums run over d and key index in ascending order.
 __global__ void __launch_bounds__(kFThreads)
 fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal) {
   extern __shared__ float fs[];
   const int D = q.dim;
-  const int DP = D + 1;
-  float* qs = fs;
-  float* ks = qs + kBlock * DP;
-  float* vs = ks + kBlock * DP;
-  float* ps = vs + kBlock * DP;  // [64][65]
-  const int blk = blockIdx.x;
+  const int QP = D + 1;
+  float* qs = fs;                 // [32][D + 1]
+  float* kt = qs + kFRows * QP;   // [D][65]: K transposed
+  float* vs = kt + D * 65;        // [64][D]
+  float* ps = vs + kBlock * D;    // [32][65]
+  const int start = blockIdx.x * kBlock;
   const int bh = blockIdx.y;
-  const int start = blk * kBlock;
+  const int r_base = blockIdx.z * kFRows;  // first query row of this CTA within the block
   const int len = min(kBlock, q.tokens - start);
-  for (int idx = threadIdx.x; idx < kBlock * D; idx += kFThreads) {
-    const int r = idx / D;
-    const int d = idx - r * D;
-    float qv = 0.f, kv = 0.f, vv = 0.f;
-    if (r < len) {
-      qv = reinterpret_cast<const float*>(q.row(bh, start + r))[d];
-      kv = reinterpret_cast<const float*>(k.row(bh, start + r))[d];
-      vv = reinterpret_cast<const float*>(v.row(bh, start + r))[d];
+  const int nr = min(kFRows, len - r_base);
+  if (nr <= 0) return;  // the whole CTA leaves before any barrier
+  const int d4n = D >> 2;
+  // K and V rows: idx -> (key c = idx % 64, 4-float group idx / 64), so the
+  // transposed K stores of a warp go to consecutive columns
+  for (int idx = threadIdx.x; idx < kBlock * d4n; idx += kFThreads) {
+    const int c = idx & 63;
+    const int d4 = (idx >> 6) << 2;
+    float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 vv4 = kv4;
+    if (c < len) {
+      kv4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(k.row(bh, start + c)) + d4);
+      vv4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(v.row(bh, start + c)) + d4);
     }
-    qs[r * DP + d] = qv;
-    ks[r * DP + d] = kv;
-    vs[r * DP + d] = vv;
+    kt[(d4 + 0) * 65 + c] = kv4.x;
+    kt[(d4 + 1) * 65 + c] = kv4.y;
+    kt[(d4 + 2) * 65 + c] = kv4.z;
+    kt[(d4 + 3) * 65 + c] = kv4.w;
+    *reinterpret_cast<float4*>(vs + c * D + d4) = vv4;
+  }
+  for (int idx = threadIdx.x; idx < kFRows * d4n; idx += kFThreads) {
+    const int r = idx / d4n;
+    const int d4 = (idx - r * d4n) << 2;
+    float4 qv4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < nr) qv4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(q.row(bh, start + r_base + r)) + d4);
+    qs[r * QP + d4 + 0] = qv4.x;
+    qs[r * QP + d4 + 1] = qv4.y;
+    qs[r * QP + d4 + 2] = qv4.z;
+    qs[r * QP + d4 + 3] = qv4.w;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < kBlock * kBlock; idx += kFThreads) {
-    const int r = idx >> 6;
-    const int c = idx & 63;
-    float acc = 0.f;
-    for (int d = 0; d < D; ++d) acc = fmaf(qs[r * DP + d], ks[c * DP + d], acc);
-    float sc = acc * scale;
-    if (c >= len || (causal && c > r)) sc = -INFINITY;
-    ps[r * 65 + c] = sc;
+  const int ty = threadIdx.x >> 4;
+  const int tx = threadIdx.x & 15;
+  const int r0 = ty;
+  const int r1 = ty + 16;
+  {
+    float s0[4] = {0.f, 0.f, 0.f, 0.f};
+    float s1[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int d = 0; d < D; ++d) {
+      const float a0 = qs[r0 * QP + d];
+      const float a1 = qs[r1 * QP + d];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float b = kt[d * 65 + tx + 16 * i];
+        s0[i] = fmaf(a0, b, s0[i]);
+        s1[i] = fmaf(a1, b, s1[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = tx + 16 * i;
+      const bool bad0 = c >= len || (causal && c > r_base + r0);
+      const bool bad1 = c >= len || (causal && c > r_base + r1);
+      ps[r0 * 65 + c] = bad0 ? -INFINITY : s0[i] * scale;
+      ps[r1 * 65 + c] = bad1 ? -INFINITY : s1[i] * scale;
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  for (int r = warp; r < kBlock; r += kFThreads / 32) {
+  for (int r = warp; r < kFRows; r += kFThreads / 32) {
     float a = ps[r * 65 + lane];
     float b = ps[r * 65 + lane + 32];
     float mx = fmaxf(a, b);
@@ -66,13 +106,30 @@ fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal) {
     ps[r * 65 + lane + 32] = b * inv;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < kBlock * D; idx += kFThreads) {
-    const int r = idx / D;
-    const int d = idx - r * D;
-    if (r >= len) continue;
-    float acc = 0.f;
-    for (int c = 0; c < len; ++c) acc = fmaf(ps[r * 65 + c], vs[c * DP + d], acc);
-    reinterpret_cast<float*>(o.row(bh, start + r))[d] = acc;
+  float o0[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float o1[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int c = 0; c < len; ++c) {
+    const float p0 = ps[r0 * 65 + c];
+    const float p1 = ps[r1 * 65 + c];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = tx + 16 * i;
+      if (d < D) {
+        const float b = vs[c * D + d];
+        o0[i] = fmaf(p0, b, o0[i]);
+        o1[i] = fmaf(p1, b, o1[i]);
+      }
+    }
+  }
+  float* out0 = r0 < nr ? reinterpret_cast<float*>(o.row(bh, start + r_base + r0)) : nullptr;
+  float* out1 = r1 < nr ? reinterpret_cast<float*>(o.row(bh, start + r_base + r1)) : nullptr;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = tx + 16 * i;
+    if (d < D) {
+      if (out0) out0[d] = o0[i];
+      if (out1) out1[d] = o1[i];
+    }
   }
 }
 
@@ -80,10 +137,11 @@ fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal) {
 
 cudaError_t launch_fixed_f32(const Rows& q, const Rows& k, const Rows& v, const Rows& o, int batch_heads,
                              float scale, int causal, cudaStream_t stream) {
-  const size_t smem = sizeof(float) * (3 * kBlock * (q.dim + 1) + kBlock * 65);
+  if (q.dim > 128 || (q.dim & 3) != 0) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float) * (kFRows * (q.dim + 1) + q.dim * 65 + kBlock * q.dim + kFRows * 65);
   cudaError_t err = ensure_smem(reinterpret_cast<const void*>(fixed_f32_kernel), static_cast<int>(smem));
   if (err != cudaSuccess) return err;
-  dim3 grid((q.tokens + kBlock - 1) / kBlock, batch_heads);
+  dim3 grid((q.tokens + kBlock - 1) / kBlock, batch_heads, kBlock / kFRows);
   fixed_f32_kernel<<<grid, kFThreads, smem, stream>>>(q, k, v, o, scale, causal);
   return cudaGetLastError();
 }

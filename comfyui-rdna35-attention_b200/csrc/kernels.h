@@ -46,6 +46,8 @@ bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const 
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,
                              const AttnParams& p, int* status, cudaStream_t stream, bool* launched);
 int* device_status_ptr();
+// Query-block pairing fits in shared memory for blocks <= 608.
+bool pair_supported(int blocks);
 cudaError_t launch_pair(const uint32_t* sel_bits, int batch_heads, int blocks, int32_t* pairs, cudaStream_t stream);
 cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype, int mode, int batch_heads,
                          int blocks, void* q_centroids, float* k_centroids, void* v_stats, float* h_sum,

@@ -9,8 +9,8 @@
 // One CTA owns 16 query blocks.  BF16 centroids (HYD): scores on the tensor
 // cores (mma.sync, FP32 accumulate) straight from global memory; FP32
 // centroids (generic): FP32 FMAs over centroids staged transposed in shared
-// memory.  Then each warp selects the top-k of two rows with k rounds of
-// warp max reductions (redux.sync) on order-preserving integer keys.
+// memory.  Then each warp selects the top-k of one row by a bitwise search
+// for the k-th largest order-preserving integer key (redux.sync counts).
 #include "common.cuh"
 
 namespace b2 {
@@ -20,7 +20,7 @@ constexpr int kRows = 16;       // query blocks per CTA
 constexpr int kThreadsR = 512;  // 16 warps: one query-block row each for the top-k
 constexpr int kRowsPerWarp = kRows / (kThreadsR / 32);
 constexpr int kFmaThreads = 256;  // FP32 path: 16 rows x 16 column lanes
-constexpr int kColChunk = 256;  // key centroids staged per pass
+constexpr int kColChunk = 128;  // key centroids staged per pass
 constexpr int kDim = 128;
 constexpr int kMaxBlocks = 1024;
 
@@ -183,29 +183,55 @@ route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict
       if (lane == 0) srow[sj] = __int_as_float(0x7f800000);
       __syncwarp();
     }
-    uint32_t taken = 0;  // bit m <-> column lane + 32*m
-    for (int round = 0; round < k; ++round) {
-      // lane's best untaken column (lowest index among equal scores), then
-      // the warp maximum and, among lanes holding it, the lowest index
-      uint32_t best = 0u;
-      uint32_t best_j = 0xffffffffu;
-      for (int m = 0, j = lane; j < blocks; ++m, j += 32) {
-        if (taken & (1u << m)) continue;
-        const uint32_t key = order_key(srow[j]);
-        if (key > best) {
-          best = key;
-          best_j = j;
-        }
-      }
-      const uint32_t wmax = __reduce_max_sync(0xffffffffu, best);
-      const uint32_t wj = __reduce_min_sync(0xffffffffu, best == wmax ? best_j : 0xffffffffu);
-      if (wj == 0xffffffffu) break;
-      if ((wj & 31) == static_cast<uint32_t>(lane)) taken |= 1u << (wj >> 5);
+    // k-th largest order key T by a bitwise search from the top bit (the
+    // largest T with at least k keys >= T); then every key > T plus the
+    // lowest-index keys == T up to k.  Lane l holds columns l + 32 m.
+    // Equivalent to k rounds of "largest remaining, lowest index on ties".
+    uint32_t key[kMaxBlocks / 32];
+    const int nm = (blocks + 31) >> 5;
+#pragma unroll
+    for (int m = 0; m < kMaxBlocks / 32; ++m) {
+      const int j = lane + 32 * m;
+      key[m] = (m < nm && j < blocks) ? order_key(srow[j]) : 0u;
     }
     uint32_t word = 0;
-    for (int w = 0; w < words; ++w) {
-      const uint32_t bits = __ballot_sync(0xffffffffu, (taken >> w) & 1u);
-      if (lane == w) word = bits;
+    if (k > 0) {
+      // a candidate with exactly k keys >= it ends the search: those k keys
+      // are the top k and every other key is strictly below them
+      uint32_t thr = 0u;
+      bool exact = false;
+      for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = thr | (1u << bit);
+        int c = 0;
+#pragma unroll
+        for (int m = 0; m < kMaxBlocks / 32; ++m)
+          if (m < nm) c += key[m] >= cand ? 1 : 0;
+        const int total = static_cast<int>(__reduce_add_sync(0xffffffffu, static_cast<unsigned>(c)));
+        if (total >= k) thr = cand;
+        if (total == k) {
+          exact = true;
+          break;
+        }
+      }
+      int gt = 0;
+#pragma unroll
+      for (int m = 0; m < kMaxBlocks / 32; ++m)
+        if (m < nm) gt += (exact ? key[m] >= thr : key[m] > thr) ? 1 : 0;
+      int need = k - static_cast<int>(__reduce_add_sync(0xffffffffu, static_cast<unsigned>(gt)));
+#pragma unroll
+      for (int m = 0; m < kMaxBlocks / 32; ++m) {
+        if (m < nm) {
+          const int j = lane + 32 * m;
+          uint32_t bits = __ballot_sync(0xffffffffu, exact ? key[m] >= thr : key[m] > thr);
+          uint32_t eq = exact ? 0u : __ballot_sync(0xffffffffu, j < blocks && key[m] == thr);
+          while (need > 0 && eq != 0u) {  // ties at the cut: lowest index first
+            bits |= eq & (~eq + 1u);
+            eq &= eq - 1u;
+            --need;
+          }
+          if (lane == m) word = bits;
+        }
+      }
     }
     const int64_t rowid = int64_t(bh) * blocks + qi;
     if (lane < words) sel_bits[rowid * words + lane] = word;
@@ -231,22 +257,58 @@ route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict
 // One warp per (batch, head): blocks are taken in ascending order; each
 // unpaired block is matched with the unpaired block of largest selection
 // overlap (ties: lowest index).  pairs[bh][p] = (a, b), b = -1 for a single.
-__global__ void __launch_bounds__(256) pair_kernel(const uint32_t* __restrict__ sel_bits, int blocks,
-                                                     int32_t* __restrict__ pairs) {
+// Only overlaps with later blocks are ever read, so they are kept as the
+// strict upper triangle: row a holds j = a+1 .. blocks-1.
+__host__ __device__ __forceinline__ int tri_row(int a, int blocks) { return a * (blocks - 1) - (a * (a - 1)) / 2; }
+// Row pitch of the selection bitsets in shared memory: odd, so that lanes
+// reading the rows of 32 consecutive blocks hit 32 different banks.
+__host__ __device__ __forceinline__ int bits_pitch(int words) { return words | 1; }
+
+constexpr int kPairThreads = 512;
+
+// Largest-overlap unpaired candidate j > a among this lane's columns
+// j = lane + 32 m (m < W, a compile-time bound so all loads issue together).
+template <int W>
+__device__ __forceinline__ uint32_t best_candidate(const uint8_t* row, int a, int blocks, int words, int lane,
+                                                   uint32_t mine) {
+  uint32_t best = 0u;
+#pragma unroll
+  for (int m = 0; m < W; ++m) {
+    const int j = (m << 5) + lane;
+    const bool cand = m < words && j > a && j < blocks && !((mine >> m) & 1u);
+    const uint32_t o = cand ? row[j] : 0u;
+    if (cand) best = max(best, (o << 16) | (0xffffu - static_cast<uint32_t>(j)));
+  }
+  return best;
+}
+
+__global__ void __launch_bounds__(kPairThreads) pair_kernel(const uint32_t* __restrict__ sel_bits, int blocks,
+                                                              int32_t* __restrict__ pairs) {
   extern __shared__ uint32_t ps[];
   const int words = (blocks + 31) >> 5;
-  uint32_t* bits = ps;                                             // [blocks][words]
-  uint8_t* ov = reinterpret_cast<uint8_t*>(bits + blocks * words);  // [blocks][blocks] overlaps (<= 255)
+  const int pitch = bits_pitch(words);
+  uint32_t* bits = ps;                                              // [blocks][pitch]
+  uint8_t* tri = reinterpret_cast<uint8_t*>(bits + blocks * pitch);  // upper-triangle overlaps (<= 255)
   const int bh = blockIdx.x;
   const int t = threadIdx.x;
-  for (int i = t; i < blocks * words; i += blockDim.x) bits[i] = sel_bits[int64_t(bh) * blocks * words + i];
+  for (int i = t; i < blocks * words; i += blockDim.x) {
+    const int r = i / words;
+    bits[r * pitch + (i - r * words)] = sel_bits[int64_t(bh) * blocks * words + i];
+  }
   __syncthreads();
-  for (int idx = t; idx < blocks * blocks; idx += blockDim.x) {
-    const int a = idx / blocks;
-    const int j = idx - a * blocks;
-    int o = 0;
-    for (int w = 0; w < words; ++w) o += __popc(bits[a * words + w] & bits[j * words + w]);
-    ov[idx] = static_cast<uint8_t>(min(o, 255));
+  {
+    const int warp = t >> 5;
+    const int lane = t & 31;
+    for (int a = warp; a < blocks - 1; a += blockDim.x >> 5) {
+      uint8_t* row = tri + tri_row(a, blocks) - (a + 1);
+      const uint32_t* ba = bits + a * pitch;
+      for (int j = a + 1 + lane; j < blocks; j += 32) {
+        const uint32_t* bj = bits + j * pitch;
+        int o = 0;
+        for (int w = 0; w < words; ++w) o += __popc(ba[w] & bj[w]);
+        row[j] = static_cast<uint8_t>(min(o, 255));
+      }
+    }
   }
   __syncthreads();
   if (t >= 32) return;
@@ -260,24 +322,9 @@ __global__ void __launch_bounds__(256) pair_kernel(const uint32_t* __restrict__ 
     if (a_used) continue;
     // candidate key = overlap << 16 | (0xffff - j): one warp max reduction
     // picks the largest overlap, ties to the lowest index; 0 = no candidate
-    uint32_t best = 0u;
-    const uint8_t* row = ov + a * blocks;
-    if (words <= 8) {
-      // fixed trip count: the byte loads of all candidate words go out together
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int j = (m << 5) + lane;
-        const bool cand = m < words && j > a && j < blocks && !((mine >> m) & 1u);
-        const uint32_t o = cand ? row[j] : 0u;
-        if (cand) best = max(best, (o << 16) | (0xffffu - static_cast<uint32_t>(j)));
-      }
-    } else {
-      for (int m = (a + 1) >> 5; (m << 5) < blocks; ++m) {
-        const int j = (m << 5) + lane;
-        if (j <= a || j >= blocks || ((mine >> m) & 1u)) continue;
-        best = max(best, (static_cast<uint32_t>(row[j]) << 16) | (0xffffu - static_cast<uint32_t>(j)));
-      }
-    }
+    const uint8_t* row = tri + tri_row(a, blocks) - (a + 1);  // row[j] valid for j > a
+    const uint32_t best = words <= 8 ? best_candidate<8>(row, a, blocks, words, lane, mine)
+                                     : best_candidate<32>(row, a, blocks, words, lane, mine);
     const uint32_t wbest = __reduce_max_sync(0xffffffffu, best);
     const int b = wbest == 0u ? -1 : static_cast<int>(0xffffu - (wbest & 0xffffu));
     if ((a & 31) == lane) mine |= 1u << (a >> 5);
@@ -293,13 +340,19 @@ __global__ void __launch_bounds__(256) pair_kernel(const uint32_t* __restrict__ 
 
 }  // namespace
 
+size_t pair_smem_bytes(int blocks) {
+  const size_t pitch = bits_pitch((blocks + 31) / 32);
+  return sizeof(uint32_t) * size_t(blocks) * pitch + size_t(blocks) * (blocks - 1) / 2;
+}
+
+bool pair_supported(int blocks) { return blocks >= 1 && blocks <= 1024 && pair_smem_bytes(blocks) <= 227 * 1024; }
+
 cudaError_t launch_pair(const uint32_t* sel_bits, int batch_heads, int blocks, int32_t* pairs, cudaStream_t stream) {
-  const int words = (blocks + 31) / 32;
-  const size_t smem = sizeof(uint32_t) * size_t(blocks) * words + size_t(blocks) * blocks;
-  if (smem > 227 * 1024 || blocks > 1024) return cudaErrorInvalidValue;
+  if (!pair_supported(blocks)) return cudaErrorInvalidValue;
+  const size_t smem = pair_smem_bytes(blocks);
   cudaError_t err = ensure_smem(reinterpret_cast<const void*>(pair_kernel), int(smem));
   if (err != cudaSuccess) return err;
-  pair_kernel<<<batch_heads, 256, smem, stream>>>(sel_bits, blocks, pairs);
+  pair_kernel<<<batch_heads, kPairThreads, smem, stream>>>(sel_bits, blocks, pairs);
   return cudaGetLastError();
 }
 

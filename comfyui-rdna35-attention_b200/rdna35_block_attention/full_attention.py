@@ -18,7 +18,7 @@ SUPPORTED_DTYPES = {torch.float16, torch.bfloat16}
 
 def _kernel_config(head_dim: int) -> dict[str, Any]:
     if head_dim == 128:
-        return {"kernel": "tcgen05", "block_m": 128, "block_n": 64, "kv_stages": 5, "softmax_warpgroups": 2}
+        return {"kernel": "tcgen05", "block_m": 128, "block_n": 64, "kv_stages": 6, "softmax_warpgroups": 2}
     return {"kernel": "mma_sync", "block_m": 64, "block_n": 64}
 
 

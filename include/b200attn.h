@@ -160,7 +160,7 @@ int b2_pisa_attention(const b2_view* q, const b2_view* k, const b2_view* v,
  * b = -1 for an unpaired block; blocks are matched greedily (ascending a) with
  * the unpaired block of largest selection overlap, so each CTA's union of
  * exact key blocks is small.  No counterpart in the reference (its
- * FlexAttention visits each query block's list separately).  nb <= 448. */
+ * FlexAttention visits each query block's list separately).  nb <= 608. */
 int b2_pisa_pair(const uint32_t* sel_bits, int32_t batch_heads, int32_t blocks,
                  int32_t* pairs, void* stream);
 

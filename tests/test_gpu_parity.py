@@ -179,6 +179,16 @@ def test_fixed_block_fp32_config1(pisa):
     assert (got - exp).abs().max().item() <= 1e-4
 
 
+@pytest.mark.parametrize("tokens,d,causal", [(200, 40, True), (1000, 128, False), (90, 64, True), (64, 8, False)])
+def test_fixed_block_fp32_ragged_causal(pisa, tokens, d, causal):
+    # T=200: the last block has 8 rows, so its second 32-row half is empty
+    gen = torch.Generator().manual_seed(tokens + d)
+    q, k, v = (torch.randn((2, 3, tokens, d), generator=gen) for _ in range(3))
+    got = pisa.fixed_block_attention(q.to(DEV), k.to(DEV), v.to(DEV), d ** -0.5, causal).cpu()
+    exp = oracle.fixed_block_attention(q, k, v, causal=causal)
+    assert (got - exp).abs().max().item() <= 1e-4
+
+
 def test_h3_pack_bit_exact(pisa):
     gen = torch.Generator().manual_seed(9170)
     qkv = torch.randn((1, 300, 3, 56, 128), generator=gen).to(torch.bfloat16).to(DEV)

@@ -92,7 +92,7 @@ def _greedy_pairs(sel):
     return pairs
 
 
-@pytest.mark.parametrize("blocks", [7, 144, 300])
+@pytest.mark.parametrize("blocks", [7, 144, 300, 512, 608])
 def test_pairing_kernel_matches_restatement(pisa, blocks):
     import ctypes
 

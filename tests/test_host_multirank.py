@@ -69,3 +69,23 @@ def test_single_process_needs_no_group():
 
     assert bench.max_over_ranks(3.5, torch.device("cpu")) == 3.5
     assert abs(bench.job_value(1, 1.0) - bench.DENSE_FLOP / 1e-3 / 1e12) < 1e-9
+
+
+def test_secondary_workloads_count_the_configs_work():
+    """Algorithmic work of the non-headline configs: dense flops 4*B*H*Tq*Tk*D
+    (configs 2, 4, 5) and the FP32 fixed-block call (config 1)."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    gflop = {name: make().value_work / 1e9 for name, make in bench.WORKLOADS.items()}
+    assert round(gflop["full_self"], 1) == 1391.6
+    assert round(gflop["full_cross"], 1) == 77.3
+    assert round(gflop["minimax_h3_t9170"], 1) == 2411.0
+    assert round(gflop["minimax_h3_t16500"], 1) == 7806.0
+    assert round(gflop["generic_pisa_video"], 1) == 21979.5
+    assert round(gflop["fixed_block_fp32"], 3) == 0.134
+    generic = bench.WORKLOADS["generic_pisa_video"]()
+    assert (generic.nb, generic.exact) == (512, 86)
+    assert round(generic.roof_work / 1e9) == round(40 * 32760 * 86 * 4 * 64 * 128 / 1e9 + 4 * 40 * 32760 * 512 * 128 / 1e9
+                                                   + 2 * 40 * 32760 * 128 * 128 / 1e9)
+    assert bench.WORKLOADS["fixed_block_fp32"]().flush
