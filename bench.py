@@ -237,16 +237,16 @@ def run_b200(args) -> None:
     ms = max_over_ranks(ms, device)
     value = job_value(world, ms)
 
-    # ---- end to end through the public API: pinned host q/k/v -> device,
-    # call, output -> pinned host, all inside the timed region
+    # ---- end to end through the public API for host-resident activations:
+    # pinned host q/k/v in, pinned host output out, all inside the timed
+    # region; forward_spatial_bhtd_host stages the call by heads so the PCIe
+    # copies overlap the compute of neighbouring stages
     out_host = torch.empty((B, T, H * D), dtype=torch.bfloat16).pin_memory()
-    dev_bthd = [torch.empty_like(h, device=device) for h in host]
+    host_bhtd = [h.permute(0, 2, 1, 3) for h in host]
 
     def e2e_step():
-        for d_, h_ in zip(dev_bthd, host):
-            d_.copy_(h_, non_blocking=True)
-        out = b200_pisa.forward_spatial_bhtd(*(x.permute(0, 2, 1, 3) for x in dev_bthd), exact_blocks=EXACT)
-        out_host.copy_(out, non_blocking=True)
+        b200_pisa.forward_spatial_bhtd_host(*host_bhtd, exact_blocks=EXACT, device=device, out=out_host,
+                                            heads_per_stage=args.heads_per_stage)
 
     for _ in range(2):
         e2e_step()
@@ -254,6 +254,21 @@ def run_b200(args) -> None:
     e2e_ms = _timed(e2e_step, max(2, args.steps // 2), stream)
     barrier()
     e2e_ms = max_over_ranks(e2e_ms, device)
+
+    # the same end-to-end call without staging (copy all in, call, copy out)
+    dev_bthd = [torch.empty_like(h, device=device) for h in host]
+
+    def serial_step():
+        for d_, h_ in zip(dev_bthd, host):
+            d_.copy_(h_, non_blocking=True)
+        out = b200_pisa.forward_spatial_bhtd(*(x.permute(0, 2, 1, 3) for x in dev_bthd), exact_blocks=EXACT)
+        out_host.copy_(out, non_blocking=True)
+
+    serial_step()
+    barrier()
+    serial_ms = max_over_ranks(_timed(serial_step, max(2, args.steps // 4), stream), device)
+    barrier()
+    del dev_bthd
     h2d = sum(h.numel() * h.element_size() for h in host)
     d2h = out_host.numel() * out_host.element_size()
 
@@ -283,7 +298,9 @@ def run_b200(args) -> None:
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) + per-tile N(0,0.5) offsets)",
             "config": CONFIG, "clocks": clock_info,
             "e2e": {"value": round(job_value(world, e2e_ms), 2), "unit": UNIT,
-                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "forward_spatial_bhtd_host", "heads_per_stage": args.heads_per_stage,
+                    "unstaged_ms_per_step": round(serial_ms, 4)},
             "gpu_launches": 6 * args.steps,
             "roofline": roofline,
         }
@@ -840,6 +857,8 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--cpu-heads", type=int, default=1)
+    parser.add_argument("--heads-per-stage", type=int, default=4,
+                        help="heads per copy/compute stage of the end-to-end (host memory) call")
     parser.add_argument("--workload", default="anima", choices=["anima", *WORKLOADS],
                         help="anima = the headline config 3; the others time the remaining configs")
     parser.add_argument("--no-cpu-baseline", action="store_true")

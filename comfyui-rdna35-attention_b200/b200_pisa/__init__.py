@@ -249,6 +249,70 @@ def forward_spatial_bhtd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exac
     return _forward_spatial_bhtd_op(q, k, v, exact_blocks, scale_value, -2 if sink_block is None else sink_block)
 
 
+def forward_spatial_bhtd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int,
+                              scale: float | None = None, sink_block: int | None = None, *,
+                              device: torch.device | int | None = None, heads_per_stage: int = 4,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+    """forward_spatial_bhtd for activations held in host memory: q/k/v are
+    BHTD views of page-locked [B,9216,H,128] BF16 raster storage on the CPU;
+    returns the [B,9216,H*128] raster output in page-locked host memory (or
+    writes ``out``).  The call runs in stages of ``heads_per_stage`` heads of
+    one batch so that the PCIe copies of one stage overlap the compute of its
+    neighbours (b2_pisa_forward_spatial_host).  Results are identical to
+    forward_spatial_bhtd on the same values.  The output is complete once the
+    device's current stream has been synchronised."""
+    if not all(isinstance(tensor, torch.Tensor) for tensor in (q, k, v)):
+        raise TypeError("q, k, and v must be torch tensors.")
+    if q.ndim != 4 or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("PISA spatial B200 expects matching [B,H,T,D] q/k/v tensors.")
+    batch, heads, tokens, head_dim = q.shape
+    if tokens != SPATIAL_TOKENS or head_dim != HEAD_DIM:
+        raise ValueError(f"PISA spatial B200 requires B>0, H>0, T={SPATIAL_TOKENS}, and D={HEAD_DIM}.")
+    if q.dtype not in _SUPPORTED_DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("PISA spatial B200 requires matching bfloat16 q/k/v.")
+    expected_stride = (tokens * heads * head_dim, head_dim, heads * head_dim, 1)
+    if q.stride() != expected_stride or k.stride() != expected_stride or v.stride() != expected_stride:
+        raise ValueError("PISA spatial B200 requires BHTD views of contiguous [B,T,H,D] storage.")
+    if any(t.is_cuda or not t.is_pinned() for t in (q, k, v)):
+        raise ValueError("host PISA requires q/k/v in page-locked (pinned) host memory.")
+    if heads_per_stage <= 0 or heads % heads_per_stage:
+        raise ValueError("heads_per_stage must divide the number of heads.")
+    blocks = SPATIAL_TOKENS // BLOCK_SIZE
+    _check_exact_and_sink(exact_blocks, blocks, sink_block)
+    if exact_blocks not in (SPATIAL_SPARSE_EXACT_BLOCKS, blocks):
+        raise ValueError(
+            f"spatial PISA supports exact_blocks={SPATIAL_SPARSE_EXACT_BLOCKS}; "
+            f"use exact_blocks={blocks} only for dense SDPA validation."
+        )
+    if device is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        dev = torch.device("cuda", device)
+    else:
+        dev = torch.device(device)
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+    _checked_device(dev.index)
+    if out is None:
+        out = torch.empty((batch, tokens, heads * head_dim), dtype=q.dtype).pin_memory()
+    elif out.shape != (batch, tokens, heads * head_dim) or not out.is_contiguous() or not out.is_pinned():
+        raise ValueError("out must be a contiguous pinned [B,T,H*D] host tensor.")
+    raster = (batch, tokens, heads, head_dim)
+    q_dev, k_dev, v_dev, o_dev = (torch.empty(raster, dtype=q.dtype, device=dev) for _ in range(4))
+    ws = _workspace(dev, heads_per_stage, tokens, exact_blocks) if exact_blocks < blocks else None
+    scale_value = _float32(1.0 / math.sqrt(HEAD_DIM) if scale is None else scale)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        check(LIB.b2_pisa_forward_spatial_host(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), q_dev.data_ptr(), k_dev.data_ptr(),
+            v_dev.data_ptr(), o_dev.data_ptr(), batch, heads, SPATIAL_SIDE, SPATIAL_SIDE, head_dim, _lib.B2_BF16,
+            exact_blocks, scale_value, -2 if sink_block is None else sink_block, heads_per_stage, ptr(ws),
+            stream.cuda_stream))
+    # the device buffers were allocated on `stream`, which waits for the last
+    # copy-out, so the caching allocator reuses them only after the copies
+    return out
+
+
 def generic_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int, scale: float,
                     first_order: bool = True, grid: tuple[int, int] | None = None,
                     out: torch.Tensor | None = None) -> torch.Tensor:

@@ -8,6 +8,7 @@
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 #include <cstring>
 
 #include "kernels.h"
@@ -55,7 +56,7 @@ cudaError_t run_stats(const b2_view* q, const b2_view* k, const b2_view* v, int 
   const int bh = q->batch * q->heads;
   const int nb = (q->tokens + kBlock - 1) / kBlock;
   if (umma_enabled()) {
-    const int group = stats_group_size(bh, nb);
+    const int group = stats_group_for_blocks(nb);
     int* status = device_status_ptr();
     bool launched = false;
     if (status != nullptr) {
@@ -207,6 +208,46 @@ int check_qkv_o(const b2_view* q, const b2_view* k, const b2_view* v, const b2_v
   if (q->dtype != k->dtype || q->dtype != v->dtype || q->dtype != o->dtype)
     return fail(B2_ERR_INVALID, "q, k, v and out must share one dtype");
   return B2_OK;
+}
+
+// Copy streams and per-stage events of the pipelined host-memory forward, one
+// set per device, created on first use and kept for the process lifetime.
+struct HostPipe {
+  cudaStream_t h2d = nullptr;
+  cudaStream_t d2h = nullptr;
+  std::vector<cudaEvent_t> ev;  // [3 * stages]: inputs in, output ready, output out
+  cudaEvent_t start = nullptr;
+};
+
+cudaError_t host_pipe(int stages, HostPipe** out) {
+  static std::mutex mu;
+  static std::map<int, HostPipe> pipes;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> lock(mu);
+  HostPipe& p = pipes[dev];
+  if (p.h2d == nullptr) {
+    if ((err = cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking)) != cudaSuccess) return err;
+    if ((err = cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking)) != cudaSuccess) return err;
+    if ((err = cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming)) != cudaSuccess) return err;
+  }
+  while (static_cast<int>(p.ev.size()) < 3 * stages) {
+    cudaEvent_t e;
+    if ((err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming)) != cudaSuccess) return err;
+    p.ev.push_back(e);
+  }
+  *out = &p;
+  return cudaSuccess;
+}
+
+bool is_pinned_host(const void* ptr) {
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return attr.type == cudaMemoryTypeHost;
 }
 
 }  // namespace
@@ -407,6 +448,80 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
   p.corr_scale = scale / static_cast<float>(q->tokens);
   err = run_attention(q, k, v, out, p, st);
   if (err != cudaSuccess) return cuda_fail(err, "PISA attention launch");
+  return ok();
+}
+
+int b2_pisa_forward_spatial_host(const void* q_host, const void* k_host, const void* v_host, void* out_host,
+                                 void* q_dev, void* k_dev, void* v_dev, void* out_dev, int32_t batch, int32_t heads,
+                                 int32_t grid_h, int32_t grid_w, int32_t head_dim, int32_t dtype,
+                                 int32_t exact_blocks, float scale, int32_t sink_block, int32_t heads_per_stage,
+                                 void* workspace, void* stream) {
+  if (!q_host || !k_host || !v_host || !out_host || !q_dev || !k_dev || !v_dev || !out_dev)
+    return fail(B2_ERR_INVALID, "host and device buffers must be non-NULL");
+  if (batch <= 0 || heads <= 0 || grid_h <= 0 || grid_w <= 0 || head_dim != 128)
+    return fail(B2_ERR_INVALID, "expected B, H > 0, a positive grid and D=128");
+  if (dtype != B2_BF16 && dtype != B2_F16) return fail(B2_ERR_UNSUPPORTED, "16-bit q/k/v only");
+  if (heads_per_stage <= 0 || heads % heads_per_stage != 0)
+    return fail(B2_ERR_INVALID, "heads_per_stage must divide heads");
+  if (!is_pinned_host(q_host) || !is_pinned_host(k_host) || !is_pinned_host(v_host) || !is_pinned_host(out_host))
+    return fail(B2_ERR_INVALID, "host buffers must be page-locked (pinned)");
+  const int32_t tokens = grid_h * grid_w;
+  const size_t es = 2;
+  const size_t pitch = size_t(heads) * head_dim * es;  // one raster row: all heads of one token
+  const size_t width = size_t(heads_per_stage) * head_dim * es;
+  const size_t batch_bytes = size_t(tokens) * pitch;
+  const int per_batch = heads / heads_per_stage;
+  const int stages = batch * per_batch;
+  HostPipe* pipe = nullptr;
+  cudaError_t err = host_pipe(stages, &pipe);
+  if (err != cudaSuccess) return cuda_fail(err, "copy stream set-up");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // copies start after the work already queued on the caller's stream
+  if ((err = cudaEventRecord(pipe->start, st)) != cudaSuccess) return cuda_fail(err, "event record");
+  if ((err = cudaStreamWaitEvent(pipe->h2d, pipe->start, 0)) != cudaSuccess) return cuda_fail(err, "stream wait");
+  if ((err = cudaStreamWaitEvent(pipe->d2h, pipe->start, 0)) != cudaSuccess) return cuda_fail(err, "stream wait");
+  for (int s = 0; s < stages; ++s) {
+    const int b = s / per_batch;
+    const int h0 = (s - b * per_batch) * heads_per_stage;
+    const size_t off = size_t(b) * batch_bytes + size_t(h0) * head_dim * es;
+    cudaEvent_t in = pipe->ev[3 * s], ready = pipe->ev[3 * s + 1];
+    const void* srcs[3] = {q_host, k_host, v_host};
+    void* dsts[3] = {q_dev, k_dev, v_dev};
+    for (int i = 0; i < 3; ++i) {
+      err = cudaMemcpy2DAsync(static_cast<char*>(dsts[i]) + off, pitch, static_cast<const char*>(srcs[i]) + off, pitch,
+                              width, tokens, cudaMemcpyHostToDevice, pipe->h2d);
+      if (err != cudaSuccess) return cuda_fail(err, "input copy");
+    }
+    if ((err = cudaEventRecord(in, pipe->h2d)) != cudaSuccess) return cuda_fail(err, "event record");
+    if ((err = cudaStreamWaitEvent(st, in, 0)) != cudaSuccess) return cuda_fail(err, "stream wait");
+    b2_view v[4];
+    void* bases[4] = {q_dev, k_dev, v_dev, out_dev};
+    for (int i = 0; i < 4; ++i) {
+      v[i].base = static_cast<char*>(bases[i]) + off;
+      v[i].stride_b = int64_t(tokens) * heads * head_dim;
+      v[i].stride_h = head_dim;
+      v[i].stride_t = int64_t(heads) * head_dim;
+      v[i].batch = 1;
+      v[i].heads = heads_per_stage;
+      v[i].tokens = tokens;
+      v[i].head_dim = head_dim;
+      v[i].dtype = dtype;
+      v[i].order = B2_ORDER_TILED8;
+      v[i].grid_h = grid_h;
+      v[i].grid_w = grid_w;
+    }
+    const int rc = b2_pisa_forward(&v[0], &v[1], &v[2], &v[3], exact_blocks, scale, sink_block, B2_STATS_HYD, 1,
+                                   workspace, stream);
+    if (rc) return rc;
+    if ((err = cudaEventRecord(ready, st)) != cudaSuccess) return cuda_fail(err, "event record");
+    if ((err = cudaStreamWaitEvent(pipe->d2h, ready, 0)) != cudaSuccess) return cuda_fail(err, "stream wait");
+    err = cudaMemcpy2DAsync(static_cast<char*>(out_host) + off, pitch, static_cast<const char*>(out_dev) + off, pitch,
+                            width, tokens, cudaMemcpyDeviceToHost, pipe->d2h);
+    if (err != cudaSuccess) return cuda_fail(err, "output copy");
+  }
+  cudaEvent_t done = pipe->ev[2];
+  if ((err = cudaEventRecord(done, pipe->d2h)) != cudaSuccess) return cuda_fail(err, "event record");
+  if ((err = cudaStreamWaitEvent(st, done, 0)) != cudaSuccess) return cuda_fail(err, "stream wait");
   return ok();
 }
 

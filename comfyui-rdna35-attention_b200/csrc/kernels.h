@@ -54,6 +54,7 @@ cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype,
                          float* h_norm, void* h_half, float* partial, cudaStream_t stream);
 int64_t stats_partial_bytes(int batch_heads, int blocks);
 int stats_group_size(int batch_heads, int blocks);
+int stats_group_for_blocks(int blocks);
 cudaError_t launch_stats_reduce(const float* partial, int groups, int batch_heads, float* h_sum, void* h_half,
                                 int dtype, cudaStream_t stream);
 cudaError_t launch_stats_umma(const b2_view& q, const b2_view& k, const b2_view& v, int mode, int group,

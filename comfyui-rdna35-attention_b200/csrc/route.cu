@@ -47,7 +47,7 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 // Scores of kRows query blocks against every key block, then per-row top-k.
 // Thread (r, cl) accumulates columns cl + 16*i of row r over d in order
 // (FP32 FMA), reading q from a broadcast row and k from a transposed chunk.
-__global__ void __launch_bounds__(kThreadsR)
+__global__ void __launch_bounds__(kThreadsR, 2)
 route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict__ kc, int kc_round_bf16,
              const float* __restrict__ h_norm, int blocks, int dim, int k, float scale, int sink,
              int32_t* __restrict__ indices, uint32_t* __restrict__ sel_bits) {
@@ -282,6 +282,27 @@ __device__ __forceinline__ uint32_t best_candidate(const uint8_t* row, int a, in
   return best;
 }
 
+// Upper-triangle overlaps popc(sel[a] & sel[j]), j > a: warp w takes rows
+// a = w, w + nwarps, ...; row a's words stay in registers.
+template <int W>
+__device__ __forceinline__ void overlap_rows(const uint32_t* bits, uint8_t* tri, int blocks, int words, int pitch,
+                                             int warp, int nwarps, int lane) {
+  for (int a = warp; a < blocks - 1; a += nwarps) {
+    uint32_t ra[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) ra[w] = w < words ? bits[a * pitch + w] : 0u;
+    uint8_t* row = tri + tri_row(a, blocks) - (a + 1);
+    for (int j = a + 1 + lane; j < blocks; j += 32) {
+      const uint32_t* bj = bits + j * pitch;
+      int o = 0;
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+        if (w < words) o += __popc(ra[w] & bj[w]);
+      row[j] = static_cast<uint8_t>(min(o, 255));
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kPairThreads) pair_kernel(const uint32_t* __restrict__ sel_bits, int blocks,
                                                               int32_t* __restrict__ pairs) {
   extern __shared__ uint32_t ps[];
@@ -296,20 +317,9 @@ __global__ void __launch_bounds__(kPairThreads) pair_kernel(const uint32_t* __re
     bits[r * pitch + (i - r * words)] = sel_bits[int64_t(bh) * blocks * words + i];
   }
   __syncthreads();
-  {
-    const int warp = t >> 5;
-    const int lane = t & 31;
-    for (int a = warp; a < blocks - 1; a += blockDim.x >> 5) {
-      uint8_t* row = tri + tri_row(a, blocks) - (a + 1);
-      const uint32_t* ba = bits + a * pitch;
-      for (int j = a + 1 + lane; j < blocks; j += 32) {
-        const uint32_t* bj = bits + j * pitch;
-        int o = 0;
-        for (int w = 0; w < words; ++w) o += __popc(ba[w] & bj[w]);
-        row[j] = static_cast<uint8_t>(min(o, 255));
-      }
-    }
-  }
+  if (words <= 8) overlap_rows<8>(bits, tri, blocks, words, pitch, t >> 5, blockDim.x >> 5, t & 31);
+  else if (words <= 16) overlap_rows<16>(bits, tri, blocks, words, pitch, t >> 5, blockDim.x >> 5, t & 31);
+  else overlap_rows<32>(bits, tri, blocks, words, pitch, t >> 5, blockDim.x >> 5, t & 31);
   __syncthreads();
   if (t >= 32) return;
   // greedy matching by one warp; lane l owns candidates j = l + 32*m and keeps

@@ -261,10 +261,16 @@ int stats_group_size(int batch_heads, int blocks) {
   return static_cast<int>(g);
 }
 
+// Blocks per work item on the workspace paths: a function of the block count
+// only, so each head's H, reduced over fixed groups in a fixed order, has the
+// same bits however many heads share the call (head-sharded or staged calls
+// reproduce the single-call output).
+int stats_group_for_blocks(int blocks) { return blocks < 16 ? (blocks < 1 ? 1 : blocks) : 16; }
+
 cudaError_t launch_stats(const Rows& q, const Rows& k, const Rows& v, int dtype, int mode, int batch_heads,
                          int blocks, void* q_centroids, float* k_centroids, void* v_stats, float* h_sum,
                          float* h_norm, void* h_half, float* partial, cudaStream_t stream) {
-  const int group = stats_group_size(batch_heads, blocks);
+  const int group = stats_group_for_blocks(blocks);
   const int groups = (blocks + group - 1) / group;
   dim3 grid(groups, batch_heads);
   const size_t smem = dtype == B2_BF16 ? sizeof(StatsSmem<__nv_bfloat16>) : sizeof(StatsSmem<__half>);
@@ -310,7 +316,7 @@ cudaError_t launch_stats_reduce(const float* partial, int groups, int batch_head
 }
 
 int64_t stats_partial_bytes(int batch_heads, int blocks) {
-  const int group = stats_group_size(batch_heads, blocks);
+  const int group = stats_group_for_blocks(blocks);
   const int groups = (blocks + group - 1) / group;
   return int64_t(batch_heads) * groups * kD * kD * 4;
 }

@@ -177,6 +177,28 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v,
                     int32_t sink_block, int32_t stats_mode,
                     int32_t first_order, void* workspace, void* stream);
 
+/* ---- Pipelined PISA HYD forward from host memory.  No counterpart in the
+ * reference (its forward_spatial_bhtd, rdna35_pisa_ck/__init__.py:406-433,
+ * takes device tensors).  q/k/v_host and out_host: page-locked raster
+ * buffers [B, grid_h*grid_w, H, 128] (BF16/FP16); q/k/v/out_dev: device
+ * buffers of the same layout.  The call runs as B*H/heads_per_stage stages
+ * of heads_per_stage heads of one batch: the inputs of a stage are copied in
+ * on a copy stream, the stage's forward (the semantics of b2_pisa_forward,
+ * B2_STATS_HYD, first-order on, tiled 8x8 token order) runs on `stream`, and
+ * its output is copied out on a second copy stream, so transfers overlap the
+ * compute of neighbouring stages.  `stream` waits for the last copy; the
+ * host output is valid once `stream` has been synchronised.  workspace:
+ * b2_pisa_workspace_bytes(heads_per_stage, T, 128, exact_blocks) bytes. */
+int b2_pisa_forward_spatial_host(const void* q_host, const void* k_host,
+                                 const void* v_host, void* out_host,
+                                 void* q_dev, void* k_dev, void* v_dev,
+                                 void* out_dev, int32_t batch, int32_t heads,
+                                 int32_t grid_h, int32_t grid_w,
+                                 int32_t head_dim, int32_t dtype,
+                                 int32_t exact_blocks, float scale,
+                                 int32_t sink_block, int32_t heads_per_stage,
+                                 void* workspace, void* stream);
+
 /* ---- Exact full attention (triton_kernel.py:113-197): out = softmax(q k^T
  * scale) v over all Tk keys, no mask.  q: [B,H,Tq,D], k/v: [B,H,Tk,D]
  * views, D in {64,128}, BF16 or FP16.  lse may be NULL. */

@@ -126,3 +126,39 @@ def test_spatial_batch_two_matches_oracle(pisa):
     exp, _ = oracle.hyd_forward_spatial(q, k, v, 23)
     assert got.shape == (2, 9216, 256)
     torch.testing.assert_close(got, exp.float(), **TOL)
+
+
+@pytest.mark.parametrize("heads_per_stage", [1, 2, 4])
+def test_host_pipelined_forward_equals_device_forward(pisa, heads_per_stage):
+    # staged copies + per-stage forwards give the same bits as one device call
+    q, k, v = oracle.anima_inputs(batch=2, heads=4, seed=17)
+    host = [x.permute(0, 2, 1, 3).contiguous().pin_memory().permute(0, 2, 1, 3) for x in (q, k, v)]
+    dev = [to_dev_bhtd(x) for x in (q, k, v)]
+    exp = pisa.forward_spatial_bhtd(*dev, exact_blocks=23).cpu()
+    out = pisa.forward_spatial_bhtd_host(*host, exact_blocks=23, heads_per_stage=heads_per_stage)
+    torch.cuda.synchronize()
+    assert out.shape == (2, 9216, 512) and out.is_pinned()
+    assert torch.equal(out, exp)
+    # and again into the same pinned output, as a sampling loop would
+    out.zero_()
+    pisa.forward_spatial_bhtd_host(*host, exact_blocks=23, heads_per_stage=heads_per_stage, out=out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, exp)
+
+
+def test_host_pipelined_forward_rejects_pageable_inputs(pisa):
+    q, k, v = oracle.anima_inputs(batch=1, heads=2, seed=1)
+    with pytest.raises(ValueError, match="pinned"):
+        pisa.forward_spatial_bhtd_host(q, k, v, exact_blocks=23)
+
+
+def test_output_of_a_head_does_not_depend_on_the_other_heads(pisa):
+    # statistics group blocks by the block count only, so a head computed
+    # alone or with others (sharded, staged) gives the same bits
+    q, k, v = oracle.generic_inputs(6, 9216, 23)
+    qd, kd, vd = (x.to(DEV) for x in (q, k, v))
+    full = pisa.forward(qd, kd, vd, exact_blocks=23)
+    part = pisa.forward(qd[2:4].contiguous(), kd[2:4].contiguous(), vd[2:4].contiguous(), exact_blocks=23)
+    one = pisa.forward(qd[5:6].contiguous(), kd[5:6].contiguous(), vd[5:6].contiguous(), exact_blocks=23)
+    assert torch.equal(part, full[2:4])
+    assert torch.equal(one, full[5:6])
