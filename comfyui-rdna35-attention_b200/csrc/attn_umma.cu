@@ -13,30 +13,36 @@
 //   * fixed block (mode DIAG): each query block's own key block
 //     (triton_kernel.py:53-100, optional causal mask).
 //
-// Warp roles (384 threads, one CTA per SM):
-//   warp 0    TMA producer: Q pair once, then K (or centroid) tiles into a
-//             6-stage ring, finally H (first-order operand) for the correction
-//   warp 10   TMA producer of the V tiles (own 6-stage ring)
-//   warps 1 / 11  single-thread MMA issuers, one per softmax warpgroup (warp 1
-//             also owns the 512 TMEM columns):
-//             S(j) = Q K(j)^T  -> TMEM S buffer of warpgroup j%2 (128 x 64 FP32,
-//                                 two buffers per warpgroup)
-//             O   += P(j) V(j) -> TMEM O of warpgroup j%2 (128 x 128 FP32),
+// Two layouts, chosen by NW (softmax warpgroups per CTA):
+//   NW = 1 (default): 224 threads, 256 TMEM columns, 2-stage K/V rings,
+//     two CTAs per SM -- one CTA's set-up (barriers, TMEM, union list, Q
+//     load, pipeline fill) and epilogue overlap the other CTA's main loop.
+//   NW = 2: 384 threads, 512 TMEM columns, 6-stage rings, one CTA per SM;
+//     the two warpgroups split the key tiles (split K inside the CTA) and
+//     merge their partial softmaxes at the end.
+// Warp roles:
+//   warp 0    TMA producer: Q pair once, then K (or centroid) tiles into the
+//             K ring, finally H (first-order operand) for the correction
+//   warp 2+4NW  TMA producer of the V tiles (own ring)
+//   warp 1 (and 11 when NW = 2)  single-thread MMA issuer per softmax
+//             warpgroup (warp 1 also owns the TMEM columns):
+//             S(j) = Q K(j)^T  -> TMEM S buffer of warpgroup j%NW (128 x 64
+//                                 FP32, two buffers per warpgroup)
+//             O   += P(j) V(j) -> TMEM O of warpgroup j%NW (128 x 128 FP32),
 //                                 P read from TMEM (tcgen05.mma A operand)
 //             C    = Q H       -> TMEM (reuses warpgroup 0's S columns)
-//             S(j) reuses the buffer of P(j-4), so it is issued only after
+//             S(j) reuses the buffer of P(j-2NW), so it is issued only after
 //             that P.V has completed; otherwise S and P.V go out as their
-//             operands arrive.  Separate issuers keep one warpgroup's chain
-//             from waiting behind the other's.
-//   warps 2-5 / 6-9  two softmax warpgroups taking alternate key tiles (split
-//             K inside the CTA): thread r owns query row r (TMEM lane r);
-//             reads its 64 logits with one tcgen05.ld pair, computes exp2 of
-//             the scaled logits with packed f32x2 arithmetic, keeps a lazy
-//             running max (O is rescaled in TMEM only when the max grows by
-//             more than 2^8), and writes P as 16-bit pairs back over the S
-//             columns with tcgen05.st.  At the end the two partial softmaxes
-//             are merged and (O + tail_mass * corr_scale * C) / l is stored,
-//             each warpgroup writing half of the columns.
+//             operands arrive.
+//   warps 2..1+4NW  softmax warpgroup(s): thread r owns query row r (TMEM
+//             lane r); reads its 64 logits with one tcgen05.ld pair,
+//             computes exp2 of the scaled logits with packed f32x2
+//             arithmetic, keeps a lazy running max (O is rescaled in TMEM
+//             only when the max grows by more than 2^8), and writes P as
+//             16-bit pairs back over the S columns with tcgen05.st.  At the
+//             end (O + tail_mass * corr_scale * C) / l is stored (with NW = 2
+//             after merging the two partial softmaxes, each warpgroup writing
+//             half of the columns).
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -50,8 +56,22 @@ namespace {
 
 using namespace umma;
 
-constexpr int kThreads = 384;  // K producer, 2 MMA issuers, 2 softmax warpgroups, V producer
-constexpr int kStages = 6;
+// NW = softmax warpgroups per CTA.
+//   NW = 2: 384 threads (K producer, 2 MMA issuers, 2 softmax warpgroups, V
+//           producer), 512 TMEM columns, 6-stage K/V rings, one CTA per SM.
+//   NW = 1: 224 threads (K producer, MMA issuer, 1 softmax warpgroup, V
+//           producer), 256 TMEM columns, 2-stage rings (97 KB of shared
+//           memory), two CTAs per SM: one CTA's set-up and epilogue overlap
+//           the other's main loop.
+template <int NW>
+struct Cfg {
+  static constexpr int kThreads = NW == 2 ? 384 : 224;
+  static constexpr int kStages = NW == 2 ? 6 : 2;
+  static constexpr int kVWarp = 2 + 4 * NW;  // V producer warp
+  static constexpr uint32_t kTmemCols = 256 * NW;
+  static constexpr int kCtasPerSm = NW == 2 ? 1 : 2;
+};
+constexpr int kMaxStages = 6;
 constexpr int kMaxList = 192;  // union of two selected lists
 constexpr int kMaxSelWords = 32;
 constexpr uint32_t kQBytes = 128 * 128 * 2;
@@ -59,10 +79,10 @@ constexpr uint32_t kSlotBytes = 64 * 128 * 2;  // one K or V tile (two 8 KB d-ha
 
 struct __align__(8) Misc {
   uint64_t q_full;
-  uint64_t k_full[kStages];
-  uint64_t k_empty[kStages];
-  uint64_t v_full[kStages];
-  uint64_t v_empty[kStages];
+  uint64_t k_full[kMaxStages];
+  uint64_t k_empty[kMaxStages];
+  uint64_t v_full[kMaxStages];
+  uint64_t v_empty[kMaxStages];
   uint64_t s_full[2][2];
   uint64_t p_full[2][2];  // [warpgroup][S buffer]: a warpgroup may run one tile ahead of the P.V issue
   uint64_t pv_done[2][2];  // [warpgroup][S buffer]
@@ -79,14 +99,16 @@ struct __align__(8) Misc {
   uint16_t list[kMaxList];
 };
 
+template <int NW>
 struct SmemLayout {
   static constexpr uint32_t q = 0;                 // [2 d-halves][128 rows][128 B]
   static constexpr uint32_t k = q + kQBytes;       // [stages][2 d-halves x 8 KB]
-  static constexpr uint32_t v = k + kStages * kSlotBytes;
-  static constexpr uint32_t misc = v + kStages * kSlotBytes;
+  static constexpr uint32_t v = k + Cfg<NW>::kStages * kSlotBytes;
+  static constexpr uint32_t misc = v + Cfg<NW>::kStages * kSlotBytes;
   static constexpr uint32_t total = misc + sizeof(Misc);
 };
-static_assert(SmemLayout::total <= 232448, "shared memory budget");
+static_assert(SmemLayout<2>::total <= 232448, "shared memory budget");
+static_assert(2 * (SmemLayout<1>::total + 1024) <= 233472, "two CTAs per SM");
 
 struct Tile {
   int tail;  // 1: centroid tail tile, 0: key block
@@ -159,12 +181,13 @@ __device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
 // S(j) = Q K(j)^T into the S buffer of warpgroup j%2; frees K slot on completion.
 // The buffer last held P(j-4): the caller issues S(j) only once that P.V has
 // completed (it reads P from these TMEM columns).
-template <bool BF16>
+template <bool BF16, int NW>
 __device__ __forceinline__ bool issue_s(Misc& m, char* k_s, uint32_t q_addr, uint32_t tmem, const UmmaArgs& a,
                                         volatile int* abort_flag, int j, long long* trace) {
+  constexpr int kStages = Cfg<NW>::kStages;
   const int s = j % kStages;
-  const int w = j & 1;
-  const int i = j >> 1;
+  const int w = j % NW;
+  const int i = j / NW;
   const int sb = i & 1;
   if (!mbar_wait(&m.k_full[s], (j / kStages) & 1, abort_flag, a.status, 4)) return false;
   tc_fence_after();
@@ -195,17 +218,18 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
 
 // O(w) += P(jj) V(jj) for key tile jj (warpgroup w = jj % 2); P is read from
 // TMEM, where the softmax wrote it over the tile's S columns.
-template <bool BF16>
+template <bool BF16, int NW>
 __device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, const UmmaArgs& a,
                                          volatile int* abort_flag, int jj) {
-  const int w = jj & 1;
-  const int i = jj >> 1;
+  constexpr int kStages = Cfg<NW>::kStages;
+  const int w = jj % NW;
+  const int i = jj / NW;
   const uint32_t p_tmem = tmem + w * 256 + 128 + 64 * (i & 1);
   if (!mbar_wait(&m.p_full[w][i & 1], (i >> 1) & 1, abort_flag, a.status, 2)) return false;
   if (!mbar_wait(&m.v_full[jj % kStages], (jj / kStages) & 1, abort_flag, a.status, 12)) return false;
   tc_fence_after();
   const uint32_t idesc_o = idesc_f16(128, 128, BF16, false, true);
-  const uint32_t v_addr = smem_u32(smem + SmemLayout::v + (jj % kStages) * kSlotBytes);
+  const uint32_t v_addr = smem_u32(smem + SmemLayout<NW>::v + (jj % kStages) * kSlotBytes);
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk) {
     const uint64_t db = smem_desc_sw128(v_addr + kk * 2048, 8192, 1024);
@@ -216,18 +240,20 @@ __device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, con
   return true;
 }
 
-template <bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool BF16, int NW>
+__global__ void __launch_bounds__(Cfg<NW>::kThreads, Cfg<NW>::kCtasPerSm)
 attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                  const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap kc_map,
                  const __grid_constant__ CUtensorMap vc_map, const __grid_constant__ CUtensorMap h_map,
                  const __grid_constant__ UmmaArgs a) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ __align__(1024) char smem[];
-  Misc& m = *reinterpret_cast<Misc*>(smem + SmemLayout::misc);
-  char* q_s = smem + SmemLayout::q;
-  char* k_s = smem + SmemLayout::k;
-  char* v_s = smem + SmemLayout::v;
+  constexpr int kThreads = Cfg<NW>::kThreads;
+  constexpr int kStages = Cfg<NW>::kStages;
+  Misc& m = *reinterpret_cast<Misc*>(smem + SmemLayout<NW>::misc);
+  char* q_s = smem + SmemLayout<NW>::q;
+  char* k_s = smem + SmemLayout<NW>::k;
+  char* v_s = smem + SmemLayout<NW>::v;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int pair = blockIdx.x;
@@ -339,7 +365,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       m.sel[half][w] = a.sel_bits[(int64_t(bh) * a.nqb + qblk) * words + w];
     }
   }
-  if (warp == 1) tmem_alloc<512>(&m.tmem);
+  if (warp == 1) tmem_alloc<Cfg<NW>::kTmemCols>(&m.tmem);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -379,7 +405,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         }
       }
     }
-  } else if (warp == 10) {
+  } else if (warp == Cfg<NW>::kVWarp) {
     // ------------------------------------------------------------ V producer
     if (lane == 0 && !*abort_flag) {
       tma_prefetch_desc(&v_map);
@@ -395,7 +421,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         }
       }
     }
-  } else if (warp == 1 || warp == 11) {
+  } else if (warp == 1 || (NW == 2 && warp == 11)) {
     // ------------------------------------------------------------ MMA issuers
     // One issuing thread per softmax warpgroup (tcgen05.commit tracks the
     // issuing thread's MMAs), so the two warpgroups' S -> P -> P.V chains
@@ -404,7 +430,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     if (elect_one()) {
       const int w = warp == 1 ? 0 : 1;
       const uint32_t q_addr = smem_u32(q_s);
-      const int cnt = (n - w + 1) >> 1;
+      const int cnt = (n - w + NW - 1) / NW;
       // S(i) may go out once P.V(i-2) (same S buffer) has completed and its K
       // tile is in; P.V(i) once P(i) and V(i) are.  S is preferred.
       bool ok = mbar_wait(&m.q_full, 0, abort_flag, a.status, 3);
@@ -413,19 +439,19 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       while (ok && npv < cnt) {
         bool did = false;
         if (ns < cnt) {
-          const int j = 2 * ns + w;
+          const int j = NW * ns + w;
           const bool buf_free = ns < 2 || (ns - 2 < npv && mbar_test_wait(&m.pv_done[w][ns & 1], ((ns - 2) >> 1) & 1));
           if (buf_free && mbar_test_wait(&m.k_full[j % kStages], (j / kStages) & 1)) {
-            ok = issue_s<BF16>(m, k_s, q_addr, tmem, a, abort_flag, j, trace);
+            ok = issue_s<BF16, NW>(m, k_s, q_addr, tmem, a, abort_flag, j, trace);
             ++ns;
             did = true;
           }
         }
         if (!did && ok && npv < ns) {
-          const int j = 2 * npv + w;
+          const int j = NW * npv + w;
           if (mbar_test_wait(&m.p_full[w][npv & 1], (npv >> 1) & 1) &&
               mbar_test_wait(&m.v_full[j % kStages], (j / kStages) & 1)) {
-            ok = issue_pv<BF16>(m, smem, tmem, a, abort_flag, j);
+            ok = issue_pv<BF16, NW>(m, smem, tmem, a, abort_flag, j);
             ++npv;
             did = true;
           }
@@ -471,7 +497,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       int no_abort = 0;
       mbar_wait(&m.mma_done[w], 0, &no_abort, a.status, 7);
     }
-  } else if (warp >= 2 && warp <= 9) {
+  } else if (warp >= 2 && warp < 2 + 4 * NW) {
     // ------------------------------------------------------------ softmax
     const int wg = (warp - 2) >> 2;   // 0 or 1
     const int sub = warp & 3;         // TMEM sub-partition of this warp
@@ -486,7 +512,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     const float log2_last_ = a.log2_last, scale_log2_ = a.scale_log2;
     int i = 0;
     bool ok = true;
-    for (int j = wg; j < n; j += 2, ++i) {
+    for (int j = wg; j < n; j += NW, ++i) {
       const int sb = i & 1;
       const Tile t = tile_at(a, m, j, ntail);
       const bool active = ((t.mask >> half) & 1u) != 0;
@@ -622,42 +648,50 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     }
     // ---- merge the two partial softmaxes, add the correction, store
     if (ok && i >= 1) ok = mbar_wait(&m.pv_done[wg][(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, a.status, 10);
-    // partial statistics [m | l | tail mass] x 128 rows per warpgroup go into
-    // the V ring (every P.V has completed once both warpgroups get here)
-    named_barrier_sync(1, 256);
-    float* stat_own = reinterpret_cast<float*>(v_s + wg * 2048);
-    const float* stat0 = reinterpret_cast<const float*>(v_s);
-    const float* stat1 = reinterpret_cast<const float*>(v_s + 2048);
-    stat_own[row] = mrun;
-    stat_own[128 + row] = lrun;
-    stat_own[256 + row] = tmass;
-    named_barrier_sync(1, 256);
+    float mm = mrun, a0 = 1.f, a1 = 0.f, lt = lrun, tt = tmass;
+    if constexpr (NW == 2) {
+      // partial statistics [m | l | tail mass] x 128 rows per warpgroup go
+      // into the V ring (every P.V has completed once both warpgroups get here)
+      named_barrier_sync(1, 256);
+      float* stat_own = reinterpret_cast<float*>(v_s + wg * 2048);
+      const float* stat0 = reinterpret_cast<const float*>(v_s);
+      const float* stat1 = reinterpret_cast<const float*>(v_s + 2048);
+      stat_own[row] = mrun;
+      stat_own[128 + row] = lrun;
+      stat_own[256 + row] = tmass;
+      named_barrier_sync(1, 256);
+      const float m0 = stat0[row], m1 = stat1[row];
+      mm = fmaxf(m0, m1);
+      a0 = m0 == -INFINITY ? 0.f : ex2(m0 - mm);
+      a1 = m1 == -INFINITY ? 0.f : ex2(m1 - mm);
+      lt = stat0[128 + row] * a0 + stat1[128 + row] * a1;
+      tt = stat0[256 + row] * a0 + stat1[256 + row] * a1;
+    }
     if (ok && a.has_corr) ok = mbar_wait(&m.c_full, 0, abort_flag, a.status, 11);
     tc_fence_after();
-    const float m0 = stat0[row], m1 = stat1[row];
-    const float mm = fmaxf(m0, m1);
-    const float a0 = m0 == -INFINITY ? 0.f : ex2(m0 - mm);
-    const float a1 = m1 == -INFINITY ? 0.f : ex2(m1 - mm);
-    const float lt = stat0[128 + row] * a0 + stat1[128 + row] * a1;
-    const float tt = stat0[256 + row] * a0 + stat1[256 + row] * a1;
     const bool store = ok && !*abort_flag && (half == 0 || has_b) && tq_row < a.tq;
     const float inv = lt > 0.f ? 1.f / lt : 0.f;
     const float cw = tt * a.corr_scale;
     char* orow = store ? a.o.row(bh, tq_row) : nullptr;
     const uint32_t row_base = tmem + lane_base;
 #pragma unroll 1
-    for (int c0 = wg * 64; c0 < wg * 64 + 64; c0 += 32) {
+    for (int c0 = wg * (128 / NW); c0 < (wg + 1) * (128 / NW); c0 += 32) {
+      // each warpgroup stores 128 / NW of the output columns
       uint32_t o0[32], o1[32], cr[32];
       tmem_ld32(row_base + c0, o0);
-      tmem_ld32(row_base + 256 + c0, o1);
+      if constexpr (NW == 2) tmem_ld32(row_base + 256 + c0, o1);
       if (a.has_corr) tmem_ld32(row_base + 128 + c0, cr);
       tmem_wait_ld();
       if (store) {
         uint32_t packed[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          float f0 = __uint_as_float(o0[c]) * a0 + __uint_as_float(o1[c]) * a1;
-          float f1 = __uint_as_float(o0[c + 1]) * a0 + __uint_as_float(o1[c + 1]) * a1;
+          float f0 = __uint_as_float(o0[c]) * a0;
+          float f1 = __uint_as_float(o0[c + 1]) * a0;
+          if constexpr (NW == 2) {
+            f0 = fmaf(__uint_as_float(o1[c]), a1, f0);
+            f1 = fmaf(__uint_as_float(o1[c + 1]), a1, f1);
+          }
           if (a.has_corr) {
             f0 = fmaf(__uint_as_float(cr[c]), cw, f0);
             f1 = fmaf(__uint_as_float(cr[c + 1]), cw, f1);
@@ -678,7 +712,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc<512>(tmem);
+    tmem_dealloc<Cfg<NW>::kTmemCols>(tmem);
   }
 }
 
@@ -766,6 +800,28 @@ bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const 
   return encode_fn() != nullptr;
 }
 
+// Softmax warpgroups per attention CTA: 1 (default; two CTAs per SM, measured
+// 27% faster on the Anima PISA call) or 2 (B200ATTN_ATTN_WG=2; one CTA per SM).
+int attn_warpgroups() {
+  static const int nw = [] {
+    const char* env = getenv("B200ATTN_ATTN_WG");
+    return env != nullptr && env[0] == '2' ? 2 : 1;
+  }();
+  return nw;
+}
+
+template <bool BF16, int NW>
+cudaError_t launch_nw(dim3 grid, cudaStream_t stream, const CUtensorMap& q_map, const CUtensorMap& k_map,
+                      const CUtensorMap& v_map, const CUtensorMap& kc_map, const CUtensorMap& vc_map,
+                      const CUtensorMap& h_map, const UmmaArgs& a) {
+  const int smem = static_cast<int>(SmemLayout<NW>::total);
+  const cudaError_t err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<BF16, NW>), smem);
+  if (err != cudaSuccess) return err;
+  attn_umma_kernel<BF16, NW><<<grid, Cfg<NW>::kThreads, smem, stream>>>(q_map, k_map, v_map, kc_map, vc_map, h_map,
+                                                                       a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,
                              const AttnParams& p, int* status, cudaStream_t stream, bool* launched) {
   *launched = false;
@@ -823,18 +879,15 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   } else {
     h_map = k_map;
   }
-  const size_t smem = SmemLayout::total;
   dim3 grid((a.nqb + 1) / 2, bh);
   cudaError_t err;
-  if (qv.dtype == B2_BF16) {
-    err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<true>), int(smem));
-    if (err != cudaSuccess) return err;
-    attn_umma_kernel<true><<<grid, kThreads, smem, stream>>>(q_map, k_map, v_map, kc_map, vc_map, h_map, a);
-  } else {
-    err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<false>), int(smem));
-    if (err != cudaSuccess) return err;
-    attn_umma_kernel<false><<<grid, kThreads, smem, stream>>>(q_map, k_map, v_map, kc_map, vc_map, h_map, a);
-  }
+  if (attn_warpgroups() == 1)
+    err = qv.dtype == B2_BF16 ? launch_nw<true, 1>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a)
+                              : launch_nw<false, 1>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+  else
+    err = qv.dtype == B2_BF16 ? launch_nw<true, 2>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a)
+                              : launch_nw<false, 2>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+  if (err != cudaSuccess) return err;
   *launched = true;
   return cudaGetLastError();
 }
