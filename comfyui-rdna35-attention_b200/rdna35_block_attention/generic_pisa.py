@@ -19,6 +19,7 @@ from . import device
 
 BLOCK_SIZE = 64
 MIN_TOKENS = 8192
+NATIVE_HEAD_DIM = 128  # the kernels' head dimension; smaller heads are zero-padded
 SPATIAL_BLOCK_EDGE = 8
 
 
@@ -69,7 +70,9 @@ def _unpack_video_blocks(tensor, grid_sizes):
 def generic_pisa_attention(q, k, v, *, exact_budget: float, scale: float | None = None, return_backend: bool = False,
                            use_first_order: bool = True, debug_finite: bool = False,
                            token_grid: tuple[int, int] | None = None, out=None):
-    """PISA over [BH,T,D] (or [B,H,T,D]) fp16/bf16 q/k/v on one CUDA device.
+    """PISA over [BH,T,D] (or [B,H,T,D]) fp16/bf16 q/k/v on one CUDA device,
+    D <= 128 in multiples of 8 (the reference's generic path accepts any D;
+    D > 128, e.g. SD1.5's 160, stays with the previous backend).
     token_grid=(h, w): tokens are per-frame h x w rasters read in 8x8-tile
     block order; the output stays in token order."""
     if q.ndim not in (3, 4) or q.shape != k.shape or q.shape != v.shape:
@@ -81,15 +84,32 @@ def generic_pisa_attention(q, k, v, *, exact_budget: float, scale: float | None 
         raise ValueError("generic PISA requires matching fp16/bf16 q/k/v")
     if not q.is_cuda or q.device != k.device or q.device != v.device:
         raise ValueError("generic PISA requires q/k/v on one CUDA device")
+    if head_dim > NATIVE_HEAD_DIM or head_dim % 8:
+        raise ValueError(f"B200 generic PISA supports head_dim <= {NATIVE_HEAD_DIM} in multiples of 8")
     blocks = math.ceil(tokens / BLOCK_SIZE)
     exact_blocks = min(blocks, max(1, math.ceil(exact_budget * blocks)))
     scale_value = float(scale) if scale is not None else 1.0 / math.sqrt(head_dim)
     native = device.native_module()
-    if exact_blocks == blocks:
-        if q.ndim == 3:
-            output = native.full_attention(q, k, v, scale_value, out=out)
+    if head_dim < NATIVE_HEAD_DIM:
+        # SD1.5-style heads (D = 40, 64, 80 ...): zero columns up to D = 128
+        # change no dot product, centroid, routing score or first-order term,
+        # so the padded call computes the same attention; the extra output
+        # columns are dropped
+        pad = NATIVE_HEAD_DIM - head_dim
+        qp, kp, vp = (F.pad(t, (0, pad)) for t in (q, k, v))
+        if exact_blocks == blocks:
+            padded = native.full_attention(qp, kp, vp, scale_value)
         else:
-            output = native.full_attention(q, k, v, scale_value, out=out)
+            padded = native.generic_forward(qp, kp, vp, exact_blocks, scale_value, first_order=use_first_order,
+                                            grid=token_grid)
+        output = padded[..., :head_dim]
+        if out is not None:
+            out.copy_(output)
+            output = out
+        backend = "dense_b200" if exact_blocks == blocks else ("b200_hyd" if use_first_order else "b200_0th")
+        return (output, backend) if return_backend else output
+    if exact_blocks == blocks:
+        output = native.full_attention(q, k, v, scale_value, out=out)
         return (output, "dense_b200") if return_backend else output
     output = native.generic_forward(q, k, v, exact_blocks, scale_value, first_order=use_first_order,
                                     grid=token_grid, out=out)

@@ -7,6 +7,7 @@ from unittest import mock
 
 import pytest
 import torch
+import torch.nn.functional as F
 
 import pisa_oracle as oracle
 from gpu_util import DEV
@@ -110,3 +111,54 @@ def test_anima_attn_op_end_to_end():
     out = op(*(x.to(DEV) for x in bshd)).cpu()
     exp, _ = oracle.hyd_forward_spatial(q[:, :2], k[:, :2], v[:, :2], 23)
     torch.testing.assert_close(out[:, :, :256].float(), exp.float(), **TOL)
+
+
+@pytest.mark.parametrize("head_dim,dtype,first_order", [(40, torch.bfloat16, False), (80, torch.bfloat16, False),
+                                                        (64, torch.float16, False), (40, torch.bfloat16, True)])
+def test_generic_pisa_small_head_dims_match_oracle(head_dim, dtype, first_order):
+    # SD1.5-style heads run zero-padded to D=128 (same attention, extra columns dropped)
+    from rdna35_block_attention.generic_pisa import generic_pisa_attention
+
+    tokens, bh = 8320, 2
+    gen = torch.Generator().manual_seed(head_dim)
+    q, k, v = (torch.randn((bh, tokens, head_dim), generator=gen).to(dtype) for _ in range(3))
+    out, backend = generic_pisa_attention(q.to(DEV), k.to(DEV), v.to(DEV), exact_budget=0.125, return_backend=True,
+                                          use_first_order=first_order)
+    assert backend == ("b200_hyd" if first_order else "b200_0th")
+    assert out.shape == (bh, tokens, head_dim)
+    exp, _ = oracle.generic_forward(q, k, v, math.ceil(0.125 * math.ceil(tokens / 64)), use_first_order=first_order)
+    torch.testing.assert_close(out.cpu().float(), exp.float(), atol=5e-2, rtol=5e-2)
+
+
+def test_generic_pisa_small_head_dim_dense_budget_matches_sdpa():
+    from rdna35_block_attention.generic_pisa import generic_pisa_attention
+
+    gen = torch.Generator().manual_seed(1)
+    q, k, v = (torch.randn((1, 2, 8192, 40), generator=gen).to(torch.bfloat16).to(DEV) for _ in range(3))
+    out, backend = generic_pisa_attention(q, k, v, exact_budget=1.0, return_backend=True)
+    assert backend == "dense_b200"
+    exp = F.scaled_dot_product_attention(q.float(), k.float(), v.float())
+    torch.testing.assert_close(out.float(), exp, atol=2e-2, rtol=2e-2)
+
+
+def test_generic_override_runs_d80_natively_and_d160_falls_back():
+    from rdna35_block_attention.generic_pisa import make_generic_pisa_override
+
+    tokens, heads = 8320, 2
+    state = _state()
+    override = make_generic_pisa_override(exact_budget=0.125, device_index=0, previous_override=None,
+                                          runtime_state=state)
+    gen = torch.Generator().manual_seed(80)
+    q, k, v = (torch.randn((1, tokens, heads * 80), generator=gen).to(torch.bfloat16) for _ in range(3))
+    out = override(mock.Mock(), q.to(DEV), k.to(DEV), v.to(DEV), heads, is_self_attention=True).cpu()
+    assert state.backend_counts["b200_0th"] == 1, state.report()
+    flat = [x.view(1, tokens, heads, 80).permute(0, 2, 1, 3).reshape(heads, tokens, 80) for x in (q, k, v)]
+    exact = math.ceil(0.25 * math.ceil(tokens / 64))  # budget clamp max(0.25, .) without first order
+    exp, _ = oracle.generic_forward(*flat, exact, use_first_order=False)
+    expected = exp.view(1, heads, tokens, 80).permute(0, 2, 1, 3).reshape(1, tokens, heads * 80)
+    torch.testing.assert_close(out.float(), expected.float(), atol=5e-2, rtol=5e-2)
+    # D=160 exceeds the kernels' 128: the previous backend runs it
+    q160 = torch.randn((1, tokens, heads * 160), generator=gen).to(torch.bfloat16).to(DEV)
+    original = mock.Mock(return_value="previous")
+    assert override(original, q160, q160, q160, heads, is_self_attention=True) == "previous"
+    assert any("pisa_backend_error" in r for r in state.fallback_reasons), state.report()
