@@ -60,13 +60,14 @@ using namespace umma;
 //   NW = 2: 384 threads (K producer, 2 MMA issuers, 2 softmax warpgroups, V
 //           producer), 512 TMEM columns, 6-stage K/V rings, one CTA per SM.
 //   NW = 1: 224 threads (K producer, MMA issuer, 1 softmax warpgroup, V
-//           producer), 256 TMEM columns, 2-stage rings (97 KB of shared
-//           memory), two CTAs per SM: one CTA's set-up and epilogue overlap
-//           the other's main loop.
+//           producer), 256 TMEM columns, 2-stage K and 3-stage V rings
+//           (113 KB of shared memory), two CTAs per SM: one CTA's set-up and
+//           epilogue overlap the other's main loop.
 template <int NW>
 struct Cfg {
   static constexpr int kThreads = NW == 2 ? 384 : 224;
-  static constexpr int kStages = NW == 2 ? 6 : 2;
+  static constexpr int kStagesK = NW == 2 ? 6 : 2;  // K ring (also carries the two H halves)
+  static constexpr int kStagesV = NW == 2 ? 6 : 3;  // V ring: P.V(j) needs V(j) one tile later than S(j) needs K(j)
   static constexpr int kVWarp = 2 + 4 * NW;  // V producer warp
   static constexpr uint32_t kTmemCols = 256 * NW;
   static constexpr int kCtasPerSm = NW == 2 ? 1 : 2;
@@ -94,8 +95,6 @@ struct __align__(8) Misc {
   int ntiles;
   int nlist;
   uint32_t sel[2][kMaxSelWords];
-  uint32_t ua[kMaxSelWords];  // selected-block bitsets of the two query blocks (list building)
-  uint32_t ub[kMaxSelWords];
   uint16_t list[kMaxList];
 };
 
@@ -103,8 +102,8 @@ template <int NW>
 struct SmemLayout {
   static constexpr uint32_t q = 0;                 // [2 d-halves][128 rows][128 B]
   static constexpr uint32_t k = q + kQBytes;       // [stages][2 d-halves x 8 KB]
-  static constexpr uint32_t v = k + Cfg<NW>::kStages * kSlotBytes;
-  static constexpr uint32_t misc = v + Cfg<NW>::kStages * kSlotBytes;
+  static constexpr uint32_t v = k + Cfg<NW>::kStagesK * kSlotBytes;
+  static constexpr uint32_t misc = v + Cfg<NW>::kStagesV * kSlotBytes;
   static constexpr uint32_t total = misc + sizeof(Misc);
 };
 static_assert(SmemLayout<2>::total <= 232448, "shared memory budget");
@@ -184,7 +183,7 @@ __device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
 template <bool BF16, int NW>
 __device__ __forceinline__ bool issue_s(Misc& m, char* k_s, uint32_t q_addr, uint32_t tmem, const UmmaArgs& a,
                                         volatile int* abort_flag, int j, long long* trace) {
-  constexpr int kStages = Cfg<NW>::kStages;
+  constexpr int kStages = Cfg<NW>::kStagesK;
   const int s = j % kStages;
   const int w = j % NW;
   const int i = j / NW;
@@ -220,8 +219,8 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
 // TMEM, where the softmax wrote it over the tile's S columns.
 template <bool BF16, int NW>
 __device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, const UmmaArgs& a,
-                                         volatile int* abort_flag, int jj) {
-  constexpr int kStages = Cfg<NW>::kStages;
+                                         volatile int* abort_flag, int jj, long long* trace) {
+  constexpr int kStages = Cfg<NW>::kStagesV;
   const int w = jj % NW;
   const int i = jj / NW;
   const uint32_t p_tmem = tmem + w * 256 + 128 + 64 * (i & 1);
@@ -237,6 +236,7 @@ __device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, con
   }
   mma_commit(&m.pv_done[w][i & 1]);
   mma_commit(&m.v_empty[jj % kStages]);
+  if (trace && jj < 256) trace[6 * 256 + 1 + jj] = clock64();
   return true;
 }
 
@@ -249,7 +249,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   extern __shared__ __align__(1024) char smem[];
   constexpr int kThreads = Cfg<NW>::kThreads;
-  constexpr int kStages = Cfg<NW>::kStages;
+  constexpr int kStagesK = Cfg<NW>::kStagesK;
+  constexpr int kStagesV = Cfg<NW>::kStagesV;
   Misc& m = *reinterpret_cast<Misc*>(smem + SmemLayout<NW>::misc);
   char* q_s = smem + SmemLayout<NW>::q;
   char* k_s = smem + SmemLayout<NW>::k;
@@ -277,9 +278,11 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       m.abort_flag = 0;
     }
     mbar_init(&m.q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kStagesK; ++s) {
       mbar_init(&m.k_full[s], 1);
       mbar_init(&m.k_empty[s], 1);
+    }
+    for (int s = 0; s < kStagesV; ++s) {
       mbar_init(&m.v_full[s], 1);
       mbar_init(&m.v_empty[s], 1);
     }
@@ -317,24 +320,28 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     // word l at the offset given by a warp prefix sum of the popcounts
     const int nbk = (a.tk + 63) / 64;
     const int wk = (nbk + 31) >> 5;
+    // scratch bitsets in the V ring, which no TMA writes before the set-up
+    // barrier below
+    uint32_t* ua = reinterpret_cast<uint32_t*>(v_s);
+    uint32_t* ub = ua + kMaxSelWords;
     if (lane < wk) {
-      m.ua[lane] = 0u;
-      m.ub[lane] = 0u;
+      ua[lane] = 0u;
+      ub[lane] = 0u;
     }
     __syncwarp();
     const int32_t* la = a.indices + (int64_t(bh) * a.nqb + qa) * a.nsel;
     const int32_t* lb = a.indices + (int64_t(bh) * a.nqb + (has_b ? qb : qa)) * a.nsel;
     for (int e = lane; e < a.nsel; e += 32) {
       const int va = min(max(la[e], 0), nbk - 1);
-      atomicOr(&m.ua[va >> 5], 1u << (va & 31));
+      atomicOr(&ua[va >> 5], 1u << (va & 31));
       if (has_b) {
         const int vb = min(max(lb[e], 0), nbk - 1);
-        atomicOr(&m.ub[vb >> 5], 1u << (vb & 31));
+        atomicOr(&ub[vb >> 5], 1u << (vb & 31));
       }
     }
     __syncwarp();
-    const uint32_t wa = lane < wk ? m.ua[lane] : 0u;
-    const uint32_t wb = lane < wk ? m.ub[lane] : 0u;
+    const uint32_t wa = lane < wk ? ua[lane] : 0u;
+    const uint32_t wb = lane < wk ? ub[lane] : 0u;
     uint32_t u = wa | wb;
     const int cnt = __popc(u);
     int incl = cnt;
@@ -356,6 +363,9 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       m.nlist = nlist;
       m.ntiles = ntail + nlist;
     }
+    // the scratch words are generic-proxy writes to memory that TMA (async
+    // proxy) fills after the set-up barrier
+    fence_proxy_async_smem();
   }
   if (ntail > 0) {
     for (int i = threadIdx.x; i < 2 * words; i += kThreads) {
@@ -387,8 +397,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       // key tiles 0..n-1, then the two 64-column halves of H as "tiles" n, n+1
       const int total = n + (a.has_corr ? 2 : 0);
       for (int j = 0; j < total; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(&m.k_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, a.status, 1)) break;
+        const int s = j % kStagesK;
+        if (!mbar_wait(&m.k_empty[s], ((j / kStagesK) & 1) ^ 1, abort_flag, a.status, 1)) break;
         char* slot = k_s + s * kSlotBytes;
         if (trace && j < 256) trace[6 * j] = clock64();
         if (j < n) {
@@ -410,8 +420,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     if (lane == 0 && !*abort_flag) {
       tma_prefetch_desc(&v_map);
       for (int j = 0; j < n; ++j) {
-        const int s = j % kStages;
-        if (!mbar_wait(&m.v_empty[s], ((j / kStages) & 1) ^ 1, abort_flag, a.status, 13)) break;
+        const int s = j % kStagesV;
+        if (!mbar_wait(&m.v_empty[s], ((j / kStagesV) & 1) ^ 1, abort_flag, a.status, 13)) break;
         char* slot = v_s + s * kSlotBytes;
         mbar_expect_tx(&m.v_full[s], kSlotBytes);
         const Tile t = tile_at(a, m, j, ntail);
@@ -441,7 +451,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         if (ns < cnt) {
           const int j = NW * ns + w;
           const bool buf_free = ns < 2 || (ns - 2 < npv && mbar_test_wait(&m.pv_done[w][ns & 1], ((ns - 2) >> 1) & 1));
-          if (buf_free && mbar_test_wait(&m.k_full[j % kStages], (j / kStages) & 1)) {
+          if (buf_free && mbar_test_wait(&m.k_full[j % kStagesK], (j / kStagesK) & 1)) {
             ok = issue_s<BF16, NW>(m, k_s, q_addr, tmem, a, abort_flag, j, trace);
             ++ns;
             did = true;
@@ -450,8 +460,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         if (!did && ok && npv < ns) {
           const int j = NW * npv + w;
           if (mbar_test_wait(&m.p_full[w][npv & 1], (npv >> 1) & 1) &&
-              mbar_test_wait(&m.v_full[j % kStages], (j / kStages) & 1)) {
-            ok = issue_pv<BF16, NW>(m, smem, tmem, a, abort_flag, j);
+              mbar_test_wait(&m.v_full[j % kStagesV], (j / kStagesV) & 1)) {
+            ok = issue_pv<BF16, NW>(m, smem, tmem, a, abort_flag, j, trace);
             ++npv;
             did = true;
           }
@@ -477,8 +487,8 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
         const uint32_t idesc_c = idesc_f16(128, 64, BF16, false, true);
         for (int hh = 0; ok && hh < 2; ++hh) {
           const int j = n + hh;
-          const int s = j % kStages;
-          ok = mbar_wait(&m.k_full[s], (j / kStages) & 1, abort_flag, a.status, 6);
+          const int s = j % kStagesK;
+          ok = mbar_wait(&m.k_full[s], (j / kStagesK) & 1, abort_flag, a.status, 6);
           if (!ok) break;
           tc_fence_after();
           const uint32_t h_addr = smem_u32(k_s + s * kSlotBytes);
@@ -644,6 +654,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&m.p_full[wg][sb]);
+      if (trace && lane == 0 && j < 256) trace[6 * 256 + 257 + 4 * j + sub] = clock64();
       if (trace && lane == 0 && sub == 0 && j < 256) trace[6 * j + 5] = clock64();
     }
     // ---- merge the two partial softmaxes, add the correction, store

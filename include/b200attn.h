@@ -83,7 +83,9 @@ const char* b2_last_kernel(void);
 int b2_read_status(int32_t* status);
 /* Diagnostics: when device_buffer is not NULL, later tcgen05 attention
  * launches of this process record clock64() timestamps of CTA (0,0) into it
- * ([256 tiles][6 events] + start, int64; see attn_umma.cu).  NULL disables. */
+ * ([256 tiles][6 events] + start + [256] P.V issue times + [256][4] P arrival
+ * times of the four softmax warps, int64: 2817
+ * entries; see attn_umma.cu).  NULL disables. */
 int b2_set_trace(long long* device_buffer);
 int b2_api_version(void);
 /* Writes a NUL-terminated "key=value;..." build description. */
