@@ -201,6 +201,7 @@ __device__ __forceinline__ bool issue_s(Misc& m, char* k_s, uint32_t q_addr, uin
   }
   mma_commit(&m.s_full[w][sb]);
   mma_commit(&m.k_empty[s]);
+  if (trace && j < 256) trace[6 * 256 + 1 + 256 + 1024 + j] = clock64();
   return true;
 }
 

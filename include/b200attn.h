@@ -84,7 +84,7 @@ int b2_read_status(int32_t* status);
 /* Diagnostics: when device_buffer is not NULL, later tcgen05 attention
  * launches of this process record clock64() timestamps of CTA (0,0) into it
  * ([256 tiles][6 events] + start + [256] P.V issue times + [256][4] P arrival
- * times of the four softmax warps, int64: 2817
+ * times of the four softmax warps + [256] S issue-return times, int64: 3073
  * entries; see attn_umma.cu).  NULL disables. */
 int b2_set_trace(long long* device_buffer);
 int b2_api_version(void);
