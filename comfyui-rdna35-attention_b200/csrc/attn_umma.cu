@@ -205,17 +205,6 @@ __device__ __forceinline__ bool issue_s(Misc& m, char* k_s, uint32_t q_addr, uin
   return true;
 }
 
-// D[tmem] (+)= A[tmem] * B[smem]: A is M x K, 16-bit pairs packed per 32-bit
-// column (lane = row), K = 16 per instruction = 8 columns.
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // O(w) += P(jj) V(jj) for key tile jj (warpgroup w = jj % 2); P is read from
 // TMEM, where the softmax wrote it over the tile's S columns.
 template <bool BF16, int NW>
