@@ -303,6 +303,9 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     fence_barrier_init();
     fence_proxy_async_smem();
   }
+  // launched with programmatic stream serialization: everything below reads
+  // the routing results (or the inputs) and writes the output
+  grid_dep_wait();
   if (a.mode == 1 && warp == 0) {
     // union of the two query blocks' selected key blocks, sorted, each entry
     // tagged with the half(s) that selected it: the lanes OR the (clamped)
@@ -818,9 +821,8 @@ cudaError_t launch_nw(dim3 grid, cudaStream_t stream, const CUtensorMap& q_map, 
   const int smem = static_cast<int>(SmemLayout<NW>::total);
   const cudaError_t err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<BF16, NW>), smem);
   if (err != cudaSuccess) return err;
-  attn_umma_kernel<BF16, NW><<<grid, Cfg<NW>::kThreads, smem, stream>>>(q_map, k_map, v_map, kc_map, vc_map, h_map,
-                                                                       a);
-  return cudaGetLastError();
+  return launch_pdl(attn_umma_kernel<BF16, NW>, grid, dim3(Cfg<NW>::kThreads), size_t(smem), stream, q_map, k_map,
+                    v_map, kc_map, vc_map, h_map, a);
 }
 
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,

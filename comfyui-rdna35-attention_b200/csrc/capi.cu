@@ -15,6 +15,14 @@
 
 
 namespace b2 {
+bool pdl_enabled() {
+  static const bool enabled = [] {
+    const char* env = getenv("B200ATTN_PDL");
+    return env == nullptr || strcmp(env, "0") != 0;
+  }();
+  return enabled;
+}
+
 cudaError_t ensure_smem(const void* kernel, int bytes) {
   static std::mutex mu;
   static std::map<std::pair<const void*, int>, int> done;

@@ -88,6 +88,33 @@ template <> struct Cvt<__half> {
 // and size: later launches skip the driver call.
 cudaError_t ensure_smem(const void* kernel, int bytes);
 
+// ---- Programmatic dependent launch.  Kernels after the first one of a PISA
+// call are launched with programmatic stream serialization: their blocks may
+// start (barrier set-up, TMEM allocation) while the previous kernel in the
+// stream drains, and each calls grid_dep_wait() before it reads or writes any
+// global memory that earlier stream work produces or consumes.  For an
+// ordinary launch grid_dep_wait() returns at once.  B200ATTN_PDL=0 turns the
+// attribute off.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

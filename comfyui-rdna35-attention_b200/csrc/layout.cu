@@ -75,6 +75,7 @@ template <typename T>
 __global__ void centroid_prep_kernel(const float* __restrict__ kc, const void* __restrict__ vstat, int vstat_is_sum,
                                      int blocks, int tokens, int dim, int64_t n, T* __restrict__ kc16,
                                      T* __restrict__ vc16) {
+  grid_dep_wait();
   const int64_t stride = int64_t(gridDim.x) * blockDim.x;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
     kc16[i] = Cvt<T>::from_f(kc[i]);
@@ -131,14 +132,11 @@ cudaError_t launch_centroid_prep(const float* kc, const void* vstat, int vstat_i
                                  int tokens, int dim, int dtype, void* kc16, void* vc16, cudaStream_t stream) {
   const int64_t n = int64_t(batch_heads) * blocks * dim;
   if (dtype == B2_BF16)
-    centroid_prep_kernel<__nv_bfloat16><<<grid_for(n, 256), 256, 0, stream>>>(
-        kc, vstat, vstat_is_sum, blocks, tokens, dim, n, static_cast<__nv_bfloat16*>(kc16),
-        static_cast<__nv_bfloat16*>(vc16));
-  else
-    centroid_prep_kernel<__half><<<grid_for(n, 256), 256, 0, stream>>>(kc, vstat, vstat_is_sum, blocks, tokens, dim,
-                                                                       n, static_cast<__half*>(kc16),
-                                                                       static_cast<__half*>(vc16));
-  return cudaGetLastError();
+    return launch_pdl(centroid_prep_kernel<__nv_bfloat16>, dim3(grid_for(n, 256)), dim3(256), 0, stream, kc, vstat,
+                      vstat_is_sum, blocks, tokens, dim, n, static_cast<__nv_bfloat16*>(kc16),
+                      static_cast<__nv_bfloat16*>(vc16));
+  return launch_pdl(centroid_prep_kernel<__half>, dim3(grid_for(n, 256)), dim3(256), 0, stream, kc, vstat,
+                    vstat_is_sum, blocks, tokens, dim, n, static_cast<__half*>(kc16), static_cast<__half*>(vc16));
 }
 
 }  // namespace b2

@@ -52,6 +52,7 @@ route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict
              const float* __restrict__ h_norm, int blocks, int dim, int k, float scale, int sink,
              int32_t* __restrict__ indices, uint32_t* __restrict__ sel_bits) {
   extern __shared__ __align__(16) float rs[];
+  grid_dep_wait();
   const int words = (blocks + 31) >> 5;
   const int chunk = min(kColChunk, (blocks + 15) & ~15);  // columns staged per pass
   const int pitch = chunk + 1;
@@ -306,6 +307,7 @@ __device__ __forceinline__ void overlap_rows(const uint32_t* bits, uint8_t* tri,
 __global__ void __launch_bounds__(kPairThreads) pair_kernel(const uint32_t* __restrict__ sel_bits, int blocks,
                                                               int32_t* __restrict__ pairs) {
   extern __shared__ uint32_t ps[];
+  grid_dep_wait();
   const int words = (blocks + 31) >> 5;
   const int pitch = bits_pitch(words);
   uint32_t* bits = ps;                                              // [blocks][pitch]
@@ -362,8 +364,7 @@ cudaError_t launch_pair(const uint32_t* sel_bits, int batch_heads, int blocks, i
   const size_t smem = pair_smem_bytes(blocks);
   cudaError_t err = ensure_smem(reinterpret_cast<const void*>(pair_kernel), int(smem));
   if (err != cudaSuccess) return err;
-  pair_kernel<<<batch_heads, kPairThreads, smem, stream>>>(sel_bits, blocks, pairs);
-  return cudaGetLastError();
+  return launch_pdl(pair_kernel, dim3(batch_heads), dim3(kPairThreads), smem, stream, sel_bits, blocks, pairs);
 }
 
 cudaError_t launch_route(const void* qc, int qc_dtype, const float* kc, int kc_round, const float* h_norm,
@@ -377,9 +378,8 @@ cudaError_t launch_route(const void* qc, int qc_dtype, const float* kc, int kc_r
   cudaError_t err = ensure_smem(reinterpret_cast<const void*>(route_kernel), static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   dim3 grid((blocks + kRows - 1) / kRows, batch_heads);
-  route_kernel<<<grid, kThreadsR, smem, stream>>>(qc, qc_dtype == B2_F32, kc, kc_round == B2_BF16, h_norm,
-                                                         blocks, dim, k, scale, sink, indices, sel_bits);
-  return cudaGetLastError();
+  return launch_pdl(route_kernel, grid, dim3(kThreadsR), smem, stream, qc, static_cast<int>(qc_dtype == B2_F32), kc,
+                    static_cast<int>(kc_round == B2_BF16), h_norm, blocks, dim, k, scale, sink, indices, sel_bits);
 }
 
 }  // namespace b2

@@ -229,6 +229,7 @@ stats_kernel(Rows q, Rows k, Rows v, int blocks, int group, void* q_centroids, f
 template <typename T>
 __global__ void stats_reduce_kernel(const float* __restrict__ partial, int groups, float* __restrict__ h_sum,
                                     T* __restrict__ h_half) {
+  grid_dep_wait();
   const int bh = blockIdx.y;
   const int idx4 = blockIdx.x * blockDim.x + threadIdx.x;  // float4 index within D*D
   if (idx4 >= kD * kD / 4) return;
@@ -308,11 +309,10 @@ cudaError_t launch_stats_reduce(const float* partial, int groups, int batch_head
                                 int dtype, cudaStream_t stream) {
   dim3 rgrid((kD * kD / 4 + 255) / 256, batch_heads);
   if (dtype == B2_BF16)
-    stats_reduce_kernel<__nv_bfloat16><<<rgrid, 256, 0, stream>>>(partial, groups, h_sum,
-                                                                  static_cast<__nv_bfloat16*>(h_half));
-  else
-    stats_reduce_kernel<__half><<<rgrid, 256, 0, stream>>>(partial, groups, h_sum, static_cast<__half*>(h_half));
-  return cudaGetLastError();
+    return launch_pdl(stats_reduce_kernel<__nv_bfloat16>, rgrid, dim3(256), 0, stream, partial, groups, h_sum,
+                      static_cast<__nv_bfloat16*>(h_half));
+  return launch_pdl(stats_reduce_kernel<__half>, rgrid, dim3(256), 0, stream, partial, groups, h_sum,
+                    static_cast<__half*>(h_half));
 }
 
 int64_t stats_partial_bytes(int batch_heads, int blocks) {
