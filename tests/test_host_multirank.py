@@ -89,3 +89,36 @@ def test_secondary_workloads_count_the_configs_work():
     assert round(generic.roof_work / 1e9) == round(40 * 32760 * 86 * 4 * 64 * 128 / 1e9 + 4 * 40 * 32760 * 512 * 128 / 1e9
                                                    + 2 * 40 * 32760 * 128 * 128 / 1e9)
     assert bench.WORKLOADS["fixed_block_fp32"]().flush
+
+
+def test_secondary_workload_reference_arm_prints_one_line():
+    """The reference arm of a secondary config runs the oracle on host cores
+    and prints the contract's line (impl, e2e with zero copy bytes,
+    cpu_baseline describing the same run)."""
+    import json
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    args = type("A", (), {"warmup": 1, "steps": 2})()
+    buf = io.StringIO()
+    with redirect_stdout(buf):
+        bench.run_workload_reference(args, bench.WORKLOADS["fixed_block_fp32"]())
+    lines = [ln for ln in buf.getvalue().splitlines() if ln.strip()]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["config"]["workload"] == "fixed_block_fp32"
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"] > 0
+    assert line["unit"] == "GFLOP/s" and line["higher_is_better"] is True
+
+
+def test_host_memory_call_rejects_pageable_buffers():
+    import pytest
+
+    sys.path.insert(0, str(ROOT / "comfyui-rdna35-attention_b200"))
+    import b200_pisa
+
+    x = torch.zeros((1, 9216, 2, 128), dtype=torch.bfloat16).permute(0, 2, 1, 3)
+    with pytest.raises(ValueError, match="pinned"):
+        b200_pisa.forward_spatial_bhtd_host(x, x, x, exact_blocks=23)
