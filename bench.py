@@ -12,6 +12,11 @@ path.  Timing: W untimed warm-ups, then K steps between a barrier +
 synchronize on both sides, CUDA events on the launching stream, max over
 ranks.  The inputs (226 MB of q/k/v) exceed the 126 MB L2, so no extra flush.
 
+``e2e`` is the same call for activations in pinned host memory
+(``b200_pisa.forward_spatial_bhtd_host``: the copies in and out are inside
+the timed region and overlap the compute of neighbouring head stages); the
+unstaged copy-in, call, copy-out time is reported beside it.
+
 ``--impl reference`` times the reference's PyTorch HYD path restated on the
 host CPU (oracle/pisa_oracle.py) on a bounded sample and reports the same
 metric.
