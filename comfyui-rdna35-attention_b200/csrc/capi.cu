@@ -225,9 +225,11 @@ struct HostPipe {
   cudaStream_t d2h = nullptr;
   std::vector<cudaEvent_t> ev;  // [3 * stages]: inputs in, output ready, output out
   cudaEvent_t start = nullptr;
+  std::mutex enqueue;  // one call's records and waits are enqueued at a time
 };
 
-cudaError_t host_pipe(int stages, HostPipe** out) {
+// The current device's pipe, its streams created on first use.
+cudaError_t host_pipe(HostPipe** out) {
   static std::mutex mu;
   static std::map<int, HostPipe> pipes;
   int dev = 0;
@@ -240,12 +242,18 @@ cudaError_t host_pipe(int stages, HostPipe** out) {
     if ((err = cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking)) != cudaSuccess) return err;
     if ((err = cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming)) != cudaSuccess) return err;
   }
+  *out = &p;
+  return cudaSuccess;
+}
+
+// At least 3 * stages events; the caller holds pipe.enqueue.
+cudaError_t host_pipe_events(HostPipe& p, int stages) {
   while (static_cast<int>(p.ev.size()) < 3 * stages) {
     cudaEvent_t e;
-    if ((err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming)) != cudaSuccess) return err;
+    const cudaError_t err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    if (err != cudaSuccess) return err;
     p.ev.push_back(e);
   }
-  *out = &p;
   return cudaSuccess;
 }
 
@@ -481,8 +489,12 @@ int b2_pisa_forward_spatial_host(const void* q_host, const void* k_host, const v
   const int per_batch = heads / heads_per_stage;
   const int stages = batch * per_batch;
   HostPipe* pipe = nullptr;
-  cudaError_t err = host_pipe(stages, &pipe);
+  cudaError_t err = host_pipe(&pipe);
   if (err != cudaSuccess) return cuda_fail(err, "copy stream set-up");
+  // the streams and events are shared by every call on this device: calls
+  // from several host threads enqueue one after the other
+  std::lock_guard<std::mutex> serial(pipe->enqueue);
+  if ((err = host_pipe_events(*pipe, stages)) != cudaSuccess) return cuda_fail(err, "event set-up");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   // copies start after the work already queued on the caller's stream
   if ((err = cudaEventRecord(pipe->start, st)) != cudaSuccess) return cuda_fail(err, "event record");

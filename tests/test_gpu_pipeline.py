@@ -162,3 +162,33 @@ def test_output_of_a_head_does_not_depend_on_the_other_heads(pisa):
     one = pisa.forward(qd[5:6].contiguous(), kd[5:6].contiguous(), vd[5:6].contiguous(), exact_blocks=23)
     assert torch.equal(part, full[2:4])
     assert torch.equal(one, full[5:6])
+
+
+def test_host_pipelined_forward_from_two_threads(pisa):
+    # the per-device copy streams and events are shared: concurrent calls
+    # from two host threads (each on its own compute stream) stay correct
+    import threading
+
+    q, k, v = oracle.anima_inputs(batch=1, heads=4, seed=29)
+    host = [x.permute(0, 2, 1, 3).contiguous().pin_memory().permute(0, 2, 1, 3) for x in (q, k, v)]
+    exp = pisa.forward_spatial_bhtd(*(to_dev_bhtd(x) for x in (q, k, v)), exact_blocks=23).cpu()
+    outs, errors = [None, None], []
+
+    def worker(i):
+        try:
+            stream = torch.cuda.Stream(DEV)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    outs[i] = pisa.forward_spatial_bhtd_host(*host, exact_blocks=23, heads_per_stage=1)
+                stream.synchronize()
+        except Exception as exc:  # reported below
+            errors.append(exc)
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for out in outs:
+        assert torch.equal(out, exp)
