@@ -44,6 +44,60 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Top-k of one score row (blocks <= 32 * NM), as this lane's selection word:
+// bit b of lane l's word <-> column 32 l + b.  The k-th largest order key T
+// comes from a bitwise search from the top bit (the largest T with at least
+// k keys >= T; a candidate with exactly k keys >= it ends the search: those
+// keys are the top k and every other key is strictly below them); then every
+// key > T plus the lowest-index keys == T up to k.  Lane l holds columns
+// l + 32 m.  Equivalent to k rounds of "largest remaining, lowest index on
+// ties".  NM bounds the unrolled loops (8 / 16 / 32 words of 32 columns).
+template <int NM>
+__device__ __forceinline__ uint32_t select_row(const float* srow, int blocks, int nm, int k, int lane) {
+  uint32_t key[NM];
+#pragma unroll
+  for (int m = 0; m < NM; ++m) {
+    const int j = lane + 32 * m;
+    key[m] = (m < nm && j < blocks) ? order_key(srow[j]) : 0u;
+  }
+  uint32_t thr = 0u;
+  bool exact = false;
+  for (int bit = 31; bit >= 0; --bit) {
+    const uint32_t cand = thr | (1u << bit);
+    int c = 0;
+#pragma unroll
+    for (int m = 0; m < NM; ++m)
+      if (m < nm) c += key[m] >= cand ? 1 : 0;
+    const int total = static_cast<int>(__reduce_add_sync(0xffffffffu, static_cast<unsigned>(c)));
+    if (total >= k) thr = cand;
+    if (total == k) {
+      exact = true;
+      break;
+    }
+  }
+  int gt = 0;
+#pragma unroll
+  for (int m = 0; m < NM; ++m)
+    if (m < nm) gt += (exact ? key[m] >= thr : key[m] > thr) ? 1 : 0;
+  int need = k - static_cast<int>(__reduce_add_sync(0xffffffffu, static_cast<unsigned>(gt)));
+  uint32_t word = 0;
+#pragma unroll
+  for (int m = 0; m < NM; ++m) {
+    if (m < nm) {
+      const int j = lane + 32 * m;
+      uint32_t bits = __ballot_sync(0xffffffffu, exact ? key[m] >= thr : key[m] > thr);
+      uint32_t eq = exact ? 0u : __ballot_sync(0xffffffffu, j < blocks && key[m] == thr);
+      while (need > 0 && eq != 0u) {  // ties at the cut: lowest index first
+        bits |= eq & (~eq + 1u);
+        eq &= eq - 1u;
+        --need;
+      }
+      if (lane == m) word = bits;
+    }
+  }
+  return word;
+}
+
 // Scores of kRows query blocks against every key block, then per-row top-k.
 // Thread (r, cl) accumulates columns cl + 16*i of row r over d in order
 // (FP32 FMA), reading q from a broadcast row and k from a transposed chunk.
@@ -184,55 +238,12 @@ route_kernel(const void* __restrict__ qc, int qc_is_f32, const float* __restrict
       if (lane == 0) srow[sj] = __int_as_float(0x7f800000);
       __syncwarp();
     }
-    // k-th largest order key T by a bitwise search from the top bit (the
-    // largest T with at least k keys >= T); then every key > T plus the
-    // lowest-index keys == T up to k.  Lane l holds columns l + 32 m.
-    // Equivalent to k rounds of "largest remaining, lowest index on ties".
-    uint32_t key[kMaxBlocks / 32];
     const int nm = (blocks + 31) >> 5;
-#pragma unroll
-    for (int m = 0; m < kMaxBlocks / 32; ++m) {
-      const int j = lane + 32 * m;
-      key[m] = (m < nm && j < blocks) ? order_key(srow[j]) : 0u;
-    }
     uint32_t word = 0;
     if (k > 0) {
-      // a candidate with exactly k keys >= it ends the search: those k keys
-      // are the top k and every other key is strictly below them
-      uint32_t thr = 0u;
-      bool exact = false;
-      for (int bit = 31; bit >= 0; --bit) {
-        const uint32_t cand = thr | (1u << bit);
-        int c = 0;
-#pragma unroll
-        for (int m = 0; m < kMaxBlocks / 32; ++m)
-          if (m < nm) c += key[m] >= cand ? 1 : 0;
-        const int total = static_cast<int>(__reduce_add_sync(0xffffffffu, static_cast<unsigned>(c)));
-        if (total >= k) thr = cand;
-        if (total == k) {
-          exact = true;
-          break;
-        }
-      }
-      int gt = 0;
-#pragma unroll
-      for (int m = 0; m < kMaxBlocks / 32; ++m)
-        if (m < nm) gt += (exact ? key[m] >= thr : key[m] > thr) ? 1 : 0;
-      int need = k - static_cast<int>(__reduce_add_sync(0xffffffffu, static_cast<unsigned>(gt)));
-#pragma unroll
-      for (int m = 0; m < kMaxBlocks / 32; ++m) {
-        if (m < nm) {
-          const int j = lane + 32 * m;
-          uint32_t bits = __ballot_sync(0xffffffffu, exact ? key[m] >= thr : key[m] > thr);
-          uint32_t eq = exact ? 0u : __ballot_sync(0xffffffffu, j < blocks && key[m] == thr);
-          while (need > 0 && eq != 0u) {  // ties at the cut: lowest index first
-            bits |= eq & (~eq + 1u);
-            eq &= eq - 1u;
-            --need;
-          }
-          if (lane == m) word = bits;
-        }
-      }
+      if (nm <= 8) word = select_row<8>(srow, blocks, nm, k, lane);
+      else if (nm <= 16) word = select_row<16>(srow, blocks, nm, k, lane);
+      else word = select_row<32>(srow, blocks, nm, k, lane);
     }
     const int64_t rowid = int64_t(bh) * blocks + qi;
     if (lane < words) sel_bits[rowid * words + lane] = word;
