@@ -23,7 +23,9 @@ metric.
 
 ``--workload`` selects one of the other configs instead of the headline one
 (full_self / full_cross: config 2; minimax_h3_t9170 / minimax_h3_t16500:
-config 4; generic_pisa_video: config 5; fixed_block_fp32: config 1).  Each
+config 4; generic_pisa_video: config 5; fixed_block_fp32: config 1;
+anima_layout_kernels: the standalone pack / unpack / merge kernels of
+config 3).  Each
 prints the same JSON line for its own public call, with the roofline of its
 dominant kernel and a bounded CPU sample of the oracle.
 """
@@ -448,7 +450,7 @@ class Workload:
         self.name, self.config, self.metric, self.unit = name, config, metric, unit
         self.value_work, self.roof_bound, self.roof_work = value_work, roof_bound, roof_work
         self.launches, self.flush = launches, flush
-        self.value_scale = 1e9 if unit.startswith("GFLOP") else 1e12
+        self.value_scale = 1e9 if unit.startswith(("GFLOP", "GB")) else 1e12
 
     # subclasses: host_inputs(seed) -> list of CPU tensors; views(dev) -> call
     # arguments; call(api, *args) -> output; kernel(api, *args) -> a callable
@@ -691,6 +693,71 @@ class FixedWorkload(Workload):
         return (time.perf_counter() - t0) / reps, f"the whole config, mean of {reps} calls"
 
 
+class LayoutWorkload(Workload):
+    """The standalone layout kernels of the Anima path that the reference's
+    `_C` module exposes (rows a2, a8, a9): raster -> block-major pack of
+    q/k/v (the call), block-major -> raster unpack and the LSE-weighted merge
+    epilogue (components).  All three are HBM copies; the fused PISA call
+    does not run them."""
+
+    def __init__(self):
+        row = B * H * T * D * 2
+        self.pack_bytes = 3.0 * 2 * row                           # 3 x (75.5 MB read + write)
+        self.unpack_bytes = 2.0 * row                             # 75.5 MB read + write
+        self.merge_bytes = 2.0 * row + 4.0 * B * H * T * D + 2 * 4.0 * B * H * T + row  # 304.3 + 75.5 MB
+        super().__init__("anima_layout_kernels", {"workload": "anima_layout_kernels", "batch": B, "heads": H,
+                                                  "tokens": T, "head_dim": D,
+                                                  "layout": "BHTD views of raster [B,T,H,D] <-> block-major [BH,T,D]",
+                                                  "l2": "inputs 226 MB > 126 MB L2 (no flush)"},
+                         "PISA spatial pack GB/s, B=2 H=16 T=9216 D=128 bf16", "GB/s", self.pack_bytes, "hbm",
+                         self.pack_bytes, 3)
+
+    def host_inputs(self, seed):
+        import pisa_oracle
+
+        return [x.permute(0, 2, 1, 3).contiguous() for x in pisa_oracle.anima_inputs(batch=B, heads=H, seed=seed)]
+
+    def views(self, dev):
+        return [x.permute(0, 2, 1, 3) for x in dev]
+
+    def call(self, api, q, k, v):
+        return api._C.pack_spatial_qkv(q, k, v)[0]
+
+    def kernel(self, api, q, k, v):
+        dev = q.device
+        gen = torch.Generator(device=dev).manual_seed(5)
+        bh = B * H
+        blk = torch.randn((bh, T, D), generator=gen, device=dev).to(torch.bfloat16)
+        approx = torch.randn((bh, T, D), generator=gen, device=dev).to(torch.bfloat16)
+        corr = torch.randn((bh, T, D), generator=gen, device=dev)
+        lse_e = torch.randn((bh, T), generator=gen, device=dev)
+        lse_a = torch.randn((bh, T), generator=gen, device=dev)
+
+        def pack():
+            api._C.pack_spatial_qkv(q, k, v)
+
+        def unpack():
+            api._C.unpack_spatial_output(blk, B, H)
+
+        def merge():
+            api._C.fuse_spatial_epilogue(blk, lse_e, approx, lse_a, corr, B, H)
+
+        pack.keep_alive = (q, k, v, blk, approx, corr, lse_e, lse_a)
+        pack.components = {"unpack_ms": unpack, "merge_ms": merge}
+        pack.component_bytes = {"unpack_ms": self.unpack_bytes, "merge_ms": self.merge_bytes}
+        return pack
+
+    def cpu_call(self):
+        import pisa_oracle
+
+        if not hasattr(self, "_cpu"):
+            self._cpu = [x[:, :1] for x in pisa_oracle.anima_inputs(batch=1, heads=1, seed=0)]
+        t0 = time.perf_counter()
+        for x in self._cpu:
+            pisa_oracle.pack_spatial(x)
+        return (time.perf_counter() - t0) * B * H, f"1 of {B * H} (batch, head) pairs, scaled x{B * H}"
+
+
 WORKLOADS = {
     "full_self": lambda: FullWorkload(T),
     "full_cross": lambda: FullWorkload(512),
@@ -698,6 +765,7 @@ WORKLOADS = {
     "minimax_h3_t16500": lambda: H3Workload(16500),
     "generic_pisa_video": GenericWorkload,
     "fixed_block_fp32": FixedWorkload,
+    "anima_layout_kernels": LayoutWorkload,
 }
 
 
@@ -815,7 +883,11 @@ def run_workload(args, wl) -> None:
             "roofline": {"bound": wl.roof_bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                          "frac": round(achieved / peak, 4), "peak_source": peaks["source"],
                          "kernel_ms": round(kernel_ms, 4), "traffic": None,
-                         **({"component_ms": components} if components else {})},
+                         **({"component_ms": components} if components else {}),
+                         **({"component_frac_of_hbm": {
+                             name: round(nbytes / (components[name] * 1e-3) / 1e9 / peaks["hbm"], 4)
+                             for name, nbytes in kernel.component_bytes.items()}}
+                            if hasattr(kernel, "component_bytes") else {})},
         }
         if not args.no_cpu_baseline and world == 1:
             torch.set_num_threads(os.cpu_count() or 1)
