@@ -89,6 +89,11 @@ def test_secondary_workloads_count_the_configs_work():
     assert round(generic.roof_work / 1e9) == round(40 * 32760 * 86 * 4 * 64 * 128 / 1e9 + 4 * 40 * 32760 * 512 * 128 / 1e9
                                                    + 2 * 40 * 32760 * 128 * 128 / 1e9)
     assert bench.WORKLOADS["fixed_block_fp32"]().flush
+    layout = bench.WORKLOADS["anima_layout_kernels"]()
+    mb = 2 * 16 * 9216 * 128 * 2 / 1e6  # one [B,H,T,D] bf16 tensor
+    assert abs(layout.pack_bytes / 1e6 - 6 * mb) < 1e-6            # q, k, v read + written
+    assert abs(layout.unpack_bytes / 1e6 - 2 * mb) < 1e-6
+    assert round(layout.merge_bytes / 1e6, 1) == 379.8             # 304.3 read + 75.5 written
 
 
 def test_secondary_workload_reference_arm_prints_one_line():
