@@ -59,3 +59,30 @@ def test_invalid_views_are_rejected_before_any_launch():
     rc = _lib.LIB.b2_pisa_forward(ctypes.byref(odd), ctypes.byref(odd), ctypes.byref(odd), ctypes.byref(odd), 1,
                                   0.1, -2, 0, 1, None, None)
     assert rc == _lib.B2_ERR_UNSUPPORTED
+
+
+def test_size_limits_and_host_call_arguments_are_checked_without_a_gpu():
+    from b200_pisa import _lib
+
+    lib = _lib.LIB
+    fake = ctypes.c_void_p(16)  # never dereferenced: the checks fail first
+    # pairing keeps its overlap triangle in shared memory: at most 608 blocks
+    assert lib.b2_pisa_pair(fake, 1, 609, fake, None) == _lib.B2_ERR_UNSUPPORTED
+    assert b"608" in lib.b2_last_error()
+    assert lib.b2_pisa_pair(None, 1, 144, fake, None) == _lib.B2_ERR_INVALID
+    # routing: at most 1024 blocks, sink in {-2, -1, 0}
+    assert lib.b2_pisa_route(fake, _lib.B2_BF16, fake, _lib.B2_BF16, None, 1, 1025, 128, 4, 0.1, -2, fake, fake,
+                             None) == _lib.B2_ERR_UNSUPPORTED
+    assert lib.b2_pisa_route(fake, _lib.B2_BF16, fake, _lib.B2_BF16, None, 1, 144, 128, 4, 0.1, 5, fake, fake,
+                             None) == _lib.B2_ERR_INVALID
+    # host-memory call: buffers, sizes and the stage split are validated
+    host = lib.b2_pisa_forward_spatial_host
+    assert host(None, fake, fake, fake, fake, fake, fake, fake, 2, 16, 96, 96, 128, _lib.B2_BF16, 23, 0.088, -2, 4,
+                fake, None) == _lib.B2_ERR_INVALID
+    assert host(fake, fake, fake, fake, fake, fake, fake, fake, 2, 16, 96, 96, 64, _lib.B2_BF16, 23, 0.088, -2, 4,
+                fake, None) == _lib.B2_ERR_INVALID
+    assert host(fake, fake, fake, fake, fake, fake, fake, fake, 2, 16, 96, 96, 128, _lib.B2_F32, 23, 0.088, -2, 4,
+                fake, None) == _lib.B2_ERR_UNSUPPORTED
+    assert host(fake, fake, fake, fake, fake, fake, fake, fake, 2, 16, 96, 96, 128, _lib.B2_BF16, 23, 0.088, -2, 3,
+                fake, None) == _lib.B2_ERR_INVALID
+    assert b"heads_per_stage" in lib.b2_last_error()
