@@ -268,6 +268,30 @@ bool is_pinned_host(const void* ptr) {
 
 }  // namespace
 
+namespace b2 {
+// Argument checks shared by both block-statistics entry points (the
+// workspace one and the allocation-free one): view shape, order, grid,
+// alignment, dtype, head dim, mode and output pointers.
+int check_stats_call(const b2_view* q, const b2_view* k, const b2_view* v, int mode, const void* q_centroids,
+                     const float* k_centroids, const void* v_stats, const float* h_sum) {
+  int rc;
+  if ((rc = check_view(q, "q")) || (rc = check_view(k, "k")) || (rc = check_view(v, "v"))) return rc;
+  if (!same_bht(q, k) || !same_bht(q, v)) return fail(B2_ERR_INVALID, "PISA statistics expect matching q/k/v");
+  if (q->dtype != k->dtype || q->dtype != v->dtype) return fail(B2_ERR_INVALID, "q, k and v must share one dtype");
+  if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA statistics support bfloat16 and float16");
+  if (q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "PISA statistics require D=128");
+  if (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC && mode != B2_STATS_SCALED)
+    return fail(B2_ERR_INVALID, "unknown statistics mode");
+  if (!q_centroids || !k_centroids || !v_stats || !h_sum)
+    return fail(B2_ERR_INVALID, "PISA statistics outputs and workspace must be non-NULL");
+  return B2_OK;
+}
+int report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+int report_cuda_error(cudaError_t err, const char* what) { return cuda_fail(err, what); }
+int report_ok() { return ok(); }
+bool tcgen05_kernels_enabled() { return umma_enabled(); }
+}  // namespace b2
+
 extern "C" {
 
 const char* b2_last_error(void) { return g_error; }
@@ -321,20 +345,9 @@ int64_t b2_stats_workspace_bytes(int32_t batch_heads, int32_t tokens, int32_t he
 int b2_pisa_block_stats(const b2_view* q, const b2_view* k, const b2_view* v, int32_t mode, void* q_centroids,
                         float* k_centroids, void* v_stats, float* h_sum, float* h_norm, void* h_bf16,
                         void* workspace, void* stream) {
-  int rc;
-  if ((rc = check_view(q, "q")) || (rc = check_view(k, "k")) || (rc = check_view(v, "v"))) return rc;
-  if (!same_bht(q, k) || !same_bht(q, v)) return fail(B2_ERR_INVALID, "PISA statistics expect matching q/k/v");
-  if (q->dtype != k->dtype || q->dtype != v->dtype) return fail(B2_ERR_INVALID, "q, k and v must share one dtype");
-  if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA statistics support bfloat16 and float16");
-  if (q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "PISA statistics require D=128");
-  if (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC && mode != B2_STATS_SCALED)
-    return fail(B2_ERR_INVALID, "unknown statistics mode");
-  if (!q_centroids || !k_centroids || !v_stats || !h_sum || !workspace)
-    return fail(B2_ERR_INVALID, "PISA statistics outputs and workspace must be non-NULL");
-  const int bh = q->batch * q->heads;
-  const int nb = (q->tokens + kBlock - 1) / kBlock;
-  (void)bh;
-  (void)nb;
+  int rc = check_stats_call(q, k, v, mode, q_centroids, k_centroids, v_stats, h_sum);
+  if (rc) return rc;
+  if (!workspace) return fail(B2_ERR_INVALID, "PISA statistics outputs and workspace must be non-NULL");
   const cudaError_t err = run_stats(q, k, v, mode, q_centroids, k_centroids, v_stats, h_sum, h_norm, h_bf16,
                                     static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail(err, "PISA block statistics launch");

@@ -72,4 +72,12 @@ cudaError_t launch_centroid_prep(const float* kc, const void* vstat, int vstat_i
                                  int tokens, int dim, int dtype, void* kc16, void* vc16, cudaStream_t stream);
 cudaError_t launch_fixed_f32(const Rows& q, const Rows& k, const Rows& v, const Rows& o, int batch_heads,
                              float scale, int causal, cudaStream_t stream);
+// Host-side helpers of the C ABI layer (capi.cu): the shared statistics
+// argument checks and the thread-local error string behind b2_last_error.
+int check_stats_call(const b2_view* q, const b2_view* k, const b2_view* v, int mode, const void* q_centroids,
+                     const float* k_centroids, const void* v_stats, const float* h_sum);
+int report_error(int code, const char* msg);
+int report_cuda_error(cudaError_t err, const char* what);
+int report_ok();
+bool tcgen05_kernels_enabled();
 }  // namespace b2

@@ -16,7 +16,7 @@
 #include <cstdio>
 #include <mutex>
 
-#include "common.cuh"
+#include "kernels.h"
 
 namespace b2 {
 namespace {
@@ -340,101 +340,81 @@ namespace {
 constexpr int64_t kNoAllocScratchBytes = 8ll << 20;
 static __device__ __align__(256) unsigned char g_stats_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_ptr[kMaxDevices] = {};
-
-// Device address of g_stats_scratch for the current device, looked up once per
-// device (the host-side symbol is only a stand-in and must never reach a kernel).
+// Device address of g_stats_scratch in the current device's context.  It is
+// looked up on every call: the host-side symbol is only a stand-in and must
+// never reach a kernel, and an address cached across a cudaDeviceReset would
+// point into a context that no longer exists.
 cudaError_t scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
+  void* ptr = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&ptr, g_stats_scratch);
   if (err != cudaSuccess) return err;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    err = cudaGetSymbolAddress(&ptr, g_stats_scratch);
-    if (err != cudaSuccess) return err;
-    g_scratch_ptr[dev] = ptr;
-  }
-  *out = g_scratch_ptr[dev];
+  *out = ptr;
   return cudaSuccess;
-}
-
-thread_local char g_noalloc_error[256] = "";
-
-int noalloc_fail(int code, const char* msg) {
-  snprintf(g_noalloc_error, sizeof(g_noalloc_error), "%s", msg);
-  return code;
 }
 
 }  // namespace
 }  // namespace b2
 
-extern "C" const char* b2_noalloc_last_error(void) { return b2::g_noalloc_error; }
+extern "C" const char* b2_noalloc_last_error(void) { return b2_last_error(); }
 
 extern "C" int b2_pisa_block_stats_noalloc(const b2_view* q, const b2_view* k, const b2_view* v, int32_t mode,
                                            void* q_centroids, float* k_centroids, void* v_stats, float* h_sum,
                                            float* h_norm, void* h_bf16, void* stream) {
   using namespace b2;
-  if (!q || !k || !v || !q->base || !k->base || !v->base)
-    return noalloc_fail(B2_ERR_INVALID, "q, k and v views must be non-NULL");
-  if (!q_centroids || !k_centroids || !v_stats || !h_sum)
-    return noalloc_fail(B2_ERR_INVALID, "PISA statistics outputs must be non-NULL");
-  for (const b2_view* x : {k, v})
-    if (x->batch != q->batch || x->heads != q->heads || x->tokens != q->tokens || x->head_dim != q->head_dim ||
-        x->dtype != q->dtype)
-      return noalloc_fail(B2_ERR_INVALID, "PISA statistics expect matching q/k/v");
-  if (q->batch <= 0 || q->heads <= 0 || q->tokens <= 0) return noalloc_fail(B2_ERR_INVALID, "sizes must be positive");
-  if (q->dtype != B2_BF16 && q->dtype != B2_F16)
-    return noalloc_fail(B2_ERR_UNSUPPORTED, "PISA statistics support bfloat16 and float16");
-  if (q->head_dim != 128) return noalloc_fail(B2_ERR_UNSUPPORTED, "PISA statistics require D=128");
-  if (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC && mode != B2_STATS_SCALED)
-    return noalloc_fail(B2_ERR_INVALID, "unknown statistics mode");
-  for (const b2_view* x : {q, k, v})
-    if (reinterpret_cast<uintptr_t>(x->base) % 16 || (x->stride_b * 2) % 16 || (x->stride_h * 2) % 16 ||
-        (x->stride_t * 2) % 16)
-      return noalloc_fail(B2_ERR_INVALID, "views must be 16-byte aligned with 16-byte strides");
+  // same argument checks as b2_pisa_block_stats (order, grid, alignment ...)
+  int rc = check_stats_call(q, k, v, mode, q_centroids, k_centroids, v_stats, h_sum);
+  if (rc) return rc;
   const int bh = q->batch * q->heads;
   const int blocks = (q->tokens + kBlock - 1) / kBlock;
-  // smallest blocks-per-CTA group (>= the default one) whose partial sums fit
+  // The workspace entry's grouping (by block count alone), grown only as far
+  // as the fixed array requires; a grown group sums H in another order.
   const int64_t per_group = int64_t(kD) * kD * 4;
-  int group = stats_group_size(bh, blocks);
+  int group = stats_group_for_blocks(blocks);
   while (group < blocks && int64_t(bh) * ((blocks + group - 1) / group) * per_group > kNoAllocScratchBytes) ++group;
   const int groups = (blocks + group - 1) / group;
   if (int64_t(bh) * groups * per_group > kNoAllocScratchBytes)
-    return noalloc_fail(B2_ERR_UNSUPPORTED,
+    return report_error(B2_ERR_UNSUPPORTED,
                         "b2_pisa_block_stats_noalloc: batch*heads exceeds 128, the 8 MiB scratch limit "
                         "(use b2_pisa_block_stats with a caller workspace)");
   void* scratch = nullptr;
   cudaError_t err = scratch_address(&scratch);
-  if (err != cudaSuccess) return noalloc_fail(B2_ERR_CUDA, cudaGetErrorString(err));
+  if (err != cudaSuccess) return report_cuda_error(err, "scratch address lookup");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const Rows qr = make_rows(*q), kr = make_rows(*k), vr = make_rows(*v);
   float* partial = static_cast<float*>(scratch);
-  dim3 grid(groups, bh);
-  const size_t smem = q->dtype == B2_BF16 ? sizeof(StatsSmem<__nv_bfloat16>) : sizeof(StatsSmem<__half>);
-#define B2_NOALLOC_LAUNCH(T, M)                                                                            \
-  do {                                                                                                     \
-    auto kern = stats_kernel<T, M>;                                                                        \
-    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
-    if (err == cudaSuccess)                                                                                \
-      kern<<<grid, kStatsThreads, smem, st>>>(qr, kr, vr, blocks, group, q_centroids, k_centroids, v_stats,\
-                                              h_norm, partial);                                            \
-  } while (0)
-  if (q->dtype == B2_BF16) {
-    if (mode == B2_STATS_HYD) B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_HYD);
-    else if (mode == B2_STATS_SCALED) B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_SCALED);
-    else B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_GENERIC);
-  } else {
-    if (mode == B2_STATS_HYD) B2_NOALLOC_LAUNCH(__half, B2_STATS_HYD);
-    else if (mode == B2_STATS_SCALED) B2_NOALLOC_LAUNCH(__half, B2_STATS_SCALED);
-    else B2_NOALLOC_LAUNCH(__half, B2_STATS_GENERIC);
+  bool launched = false;
+  if (tcgen05_kernels_enabled()) {
+    int* status = device_status_ptr();
+    if (status != nullptr) {
+      err = launch_stats_umma(*q, *k, *v, mode, group, q_centroids, k_centroids, v_stats, h_norm, partial, status,
+                              st, &launched);
+      if (err != cudaSuccess) return report_cuda_error(err, "PISA statistics launch");
+    }
   }
+  if (!launched) {
+    const Rows qr = make_rows(*q), kr = make_rows(*k), vr = make_rows(*v);
+    dim3 grid(groups, bh);
+    const size_t smem = q->dtype == B2_BF16 ? sizeof(StatsSmem<__nv_bfloat16>) : sizeof(StatsSmem<__half>);
+#define B2_NOALLOC_LAUNCH(T, M)                                                                              \
+  do {                                                                                                       \
+    auto kern = stats_kernel<T, M>;                                                                          \
+    err = ensure_smem(reinterpret_cast<const void*>(kern), static_cast<int>(smem));                          \
+    if (err == cudaSuccess)                                                                                  \
+      kern<<<grid, kStatsThreads, smem, st>>>(qr, kr, vr, blocks, group, q_centroids, k_centroids, v_stats,  \
+                                              h_norm, partial);                                              \
+  } while (0)
+    if (q->dtype == B2_BF16) {
+      if (mode == B2_STATS_HYD) B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_HYD);
+      else if (mode == B2_STATS_SCALED) B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_SCALED);
+      else B2_NOALLOC_LAUNCH(__nv_bfloat16, B2_STATS_GENERIC);
+    } else {
+      if (mode == B2_STATS_HYD) B2_NOALLOC_LAUNCH(__half, B2_STATS_HYD);
+      else if (mode == B2_STATS_SCALED) B2_NOALLOC_LAUNCH(__half, B2_STATS_SCALED);
+      else B2_NOALLOC_LAUNCH(__half, B2_STATS_GENERIC);
+    }
 #undef B2_NOALLOC_LAUNCH
-  if (err == cudaSuccess) err = cudaGetLastError();
-  if (err != cudaSuccess) return noalloc_fail(B2_ERR_CUDA, cudaGetErrorString(err));
+    if (err == cudaSuccess) err = cudaGetLastError();
+    if (err != cudaSuccess) return report_cuda_error(err, "PISA statistics launch");
+  }
   dim3 rgrid((kD * kD / 4 + 255) / 256, bh);
   if (q->dtype == B2_BF16)
     stats_reduce_kernel<__nv_bfloat16><<<rgrid, 256, 0, st>>>(partial, groups, h_sum,
@@ -442,7 +422,6 @@ extern "C" int b2_pisa_block_stats_noalloc(const b2_view* q, const b2_view* k, c
   else
     stats_reduce_kernel<__half><<<rgrid, 256, 0, st>>>(partial, groups, h_sum, static_cast<__half*>(h_bf16));
   err = cudaGetLastError();
-  if (err != cudaSuccess) return noalloc_fail(B2_ERR_CUDA, cudaGetErrorString(err));
-  g_noalloc_error[0] = '\0';
-  return B2_OK;
+  if (err != cudaSuccess) return report_cuda_error(err, "PISA statistics reduction launch");
+  return report_ok();
 }

@@ -108,19 +108,25 @@ int b2_pisa_block_stats(const b2_view* q, const b2_view* k, const b2_view* v,
                         void* h_bf16, void* workspace, void* stream);
 
 /* ---- Allocation-free block statistics.  No counterpart in the reference.
- * Same inputs, outputs and semantics as b2_pisa_block_stats, but the partial
- * H sums go to an 8 MiB array compiled into the library (one copy per GPU,
- * held until the process exits) instead of a caller workspace, for callers
- * that cannot allocate device memory when they run (allocator callbacks,
- * fixed memory pools, plugin hosts that only hand out input/output buffers).
+ * Same inputs, outputs and argument checks as b2_pisa_block_stats, but the
+ * partial H sums go to an 8 MiB array compiled into the library (one copy per
+ * GPU, held until the process exits) instead of a caller workspace, for
+ * callers that cannot allocate device memory when they run (allocator
+ * callbacks, fixed memory pools, plugin hosts that only hand out input/output
+ * buffers).
  * Limit: batch*heads*ceil(nb/group) partials of 64 KiB must fit in 8 MiB,
  * i.e. batch*heads <= 128; larger requests fail with B2_ERR_UNSUPPORTED.
- * The first call on each device looks up the array's device address (with
- * that device current); make that first call before any stream capture.
- * Every call shares the array and overwrites all of it that it reads, so no
- * clearing is needed, but calls whose kernels overlap on the GPU (different
- * streams or devices sharing a context) race on it.  Errors are reported by
- * b2_noalloc_last_error(). */
+ * Blocks are grouped as in b2_pisa_block_stats (so h_sum/h_bf16 match it bit
+ * for bit) unless the array forces larger groups; then H is summed in another
+ * order and matches only within FP32 reassociation.  Centroids and h_norm
+ * always match bit for bit.
+ * Every call looks up the array's device address in the current device's
+ * context (cudaGetSymbolAddress; make the first call on a device before any
+ * stream capture).  Every call shares the array and overwrites all of it that
+ * it reads, so no clearing is needed, but calls whose kernels overlap on the
+ * same GPU (different streams, or host threads) race on it.  Errors are
+ * reported by b2_last_error(); b2_noalloc_last_error() returns the same
+ * string. */
 int b2_pisa_block_stats_noalloc(const b2_view* q, const b2_view* k,
                                 const b2_view* v, int32_t mode,
                                 void* q_centroids, float* k_centroids,

@@ -86,3 +86,44 @@ def test_size_limits_and_host_call_arguments_are_checked_without_a_gpu():
     assert host(fake, fake, fake, fake, fake, fake, fake, fake, 2, 16, 96, 96, 128, _lib.B2_BF16, 23, 0.088, -2, 3,
                 fake, None) == _lib.B2_ERR_INVALID
     assert b"heads_per_stage" in lib.b2_last_error()
+
+
+def test_noalloc_statistics_share_the_view_checks():
+    """The allocation-free statistics entry runs the same view checks as the
+    workspace entry (token order, tiled grid, token count) before any launch."""
+    import torch
+    from b200_pisa import _lib
+
+    lib = _lib.LIB
+    lib.b2_pisa_block_stats_noalloc.restype = ctypes.c_int
+    lib.b2_pisa_block_stats_noalloc.argtypes = [ctypes.POINTER(_lib.View)] * 3 + [ctypes.c_int32] + [ctypes.c_void_p] * 7
+    fake = ctypes.c_void_p(256)  # never dereferenced: the checks fail first
+    x = torch.zeros((1, 2, 1024, 128), dtype=torch.bfloat16)
+
+    def call(v, entry):
+        if entry == "noalloc":
+            return lib.b2_pisa_block_stats_noalloc(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), _lib.STATS_HYD,
+                                                   fake, fake, fake, fake, None, None, None)
+        return lib.b2_pisa_block_stats(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), _lib.STATS_HYD,
+                                       fake, fake, fake, fake, None, None, fake, None)
+
+    bad_cases = {
+        "unknown token order": _lib.view(x, order=7),
+        "grid_h <= 0": _lib.view(x, order=_lib.ORDER_TILED8, grid=(0, 32)),
+        "grid not divisible by 8": _lib.view(x, order=_lib.ORDER_TILED8, grid=(12, 32)),
+        "tokens not a multiple of the frame": _lib.view(x, order=_lib.ORDER_TILED8, grid=(16, 48)),
+    }
+    for what, v in bad_cases.items():
+        for entry in ("noalloc", "workspace"):
+            assert call(v, entry) == _lib.B2_ERR_INVALID, (what, entry)
+            msg = lib.b2_last_error()
+            assert msg, (what, entry)
+    lib.b2_noalloc_last_error.restype = ctypes.c_char_p
+    assert lib.b2_noalloc_last_error() == lib.b2_last_error()
+    # an unknown statistics mode and a missing output are rejected too
+    good = _lib.view(x)
+    assert lib.b2_pisa_block_stats_noalloc(ctypes.byref(good), ctypes.byref(good), ctypes.byref(good), 9, fake, fake,
+                                           fake, fake, None, None, None) == _lib.B2_ERR_INVALID
+    assert lib.b2_pisa_block_stats_noalloc(ctypes.byref(good), ctypes.byref(good), ctypes.byref(good),
+                                           _lib.STATS_HYD, None, fake, fake, fake, None, None,
+                                           None) == _lib.B2_ERR_INVALID
