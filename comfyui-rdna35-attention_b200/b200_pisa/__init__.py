@@ -16,6 +16,7 @@ place instead of packing it.
 """
 from __future__ import annotations
 
+import ctypes
 import functools
 import math
 import struct
@@ -129,7 +130,9 @@ def _workspace(device: torch.device, batch_heads: int, tokens: int, exact_blocks
 
 
 def _native_forward(q_view, k_view, v_view, out_view, ref: torch.Tensor, batch_heads: int, tokens: int,
-                    exact_blocks: int, scale: float, sink_block: int, stats_mode: int, first_order: bool) -> None:
+                    exact_blocks: int, scale: float, sink_block: int, stats_mode: int,
+                    first_order: bool) -> torch.Tensor | None:
+    """One b2_pisa_forward call; returns the workspace it used (None when dense)."""
     _checked_device(ref.device.index if ref.device.index is not None else torch.cuda.current_device())
     blocks = (tokens + BLOCK_SIZE - 1) // BLOCK_SIZE
     workspace = _workspace(ref.device, batch_heads, tokens, exact_blocks) if exact_blocks < blocks else None
@@ -139,6 +142,46 @@ def _native_forward(q_view, k_view, v_view, out_view, ref: torch.Tensor, batch_h
             sink_block, stats_mode, 1 if first_order else 0, ptr(workspace), stream_of(ref),
         )
     )
+    return workspace
+
+
+def _routing_from_workspace(workspace: torch.Tensor, batch_heads: int, tokens: int, exact_blocks: int):
+    """(indices int32 [BH,nb,k], h_norm FP32 [BH,nb]) read from a sparse
+    b2_pisa_forward workspace at the offsets b2_pisa_workspace_layout reports."""
+    blocks = (tokens + BLOCK_SIZE - 1) // BLOCK_SIZE
+    offsets = (ctypes.c_int64 * _lib.WS_FIELDS)()
+    check(LIB.b2_pisa_workspace_layout(batch_heads, tokens, HEAD_DIM, exact_blocks, offsets, _lib.WS_FIELDS))
+
+    def field(index: int, count: int, dtype: torch.dtype) -> torch.Tensor:
+        start = offsets[index]
+        nbytes = count * torch.empty((), dtype=dtype).element_size()
+        return workspace[start:start + nbytes].view(dtype)
+
+    indices = field(_lib.WS_INDICES, batch_heads * blocks * exact_blocks, torch.int32)
+    h_norm = field(_lib.WS_HNORM, batch_heads * blocks, torch.float32)
+    return indices.view(batch_heads, blocks, exact_blocks).clone(), h_norm.view(batch_heads, blocks).clone()
+
+
+def forward_spatial_bhtd_with_routing(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int,
+                                      scale: float | None = None, sink_block: int | None = None):
+    """Diagnostics form of forward_spatial_bhtd: (output, indices, h_norm),
+    where indices int32 [B*H,144,exact_blocks] are the key blocks the call
+    routed each query block to (ascending, block-major order) and h_norm FP32
+    [B*H,144] the covariance norms behind the routing bias.  Same kernels and
+    output as forward_spatial_bhtd; sparse calls only."""
+    _validate_spatial_bhtd(q, k, v)
+    blocks = SPATIAL_TOKENS // BLOCK_SIZE
+    _check_exact_and_sink(exact_blocks, blocks, sink_block)
+    if not 0 < exact_blocks < blocks:
+        raise ValueError("routing is only produced by sparse calls (0 < exact_blocks < 144).")
+    scale_value = _float32(1.0 / math.sqrt(HEAD_DIM) if scale is None else scale)
+    batch, heads, tokens, head_dim = q.shape
+    out = torch.empty((batch, tokens, heads * head_dim), device=q.device, dtype=q.dtype)
+    qv, kv, vv, ov = _spatial_views(q, k, v, out)
+    ws = _native_forward(qv, kv, vv, ov, q, batch * heads, tokens, exact_blocks, scale_value,
+                         -2 if sink_block is None else sink_block, _lib.STATS_HYD, True)
+    indices, h_norm = _routing_from_workspace(ws, batch * heads, tokens, exact_blocks)
+    return out, indices, h_norm
 
 
 def ctypes_ref(v):
@@ -315,13 +358,15 @@ def forward_spatial_bhtd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 def generic_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int, scale: float,
                     first_order: bool = True, grid: tuple[int, int] | None = None,
-                    out: torch.Tensor | None = None) -> torch.Tensor:
+                    out: torch.Tensor | None = None, return_indices: bool = False):
     """Generic PISA (generic_pisa.py:141-232 semantics): FP32 centroids,
     routing without the HYD bias, 16-bit-rounded centred K, optional
     first-order term.  q/k/v: [BH,T,128] or [B,H,T,128] views (fp16/bf16,
     head dimension contiguous), T up to 65536.  grid=(h, w) reads the tokens
     in 8x8-tile order of per-frame h x w rasters (no packing copy); the
-    output (``out`` view or a new tensor shaped like q) is in token order."""
+    output (``out`` view or a new tensor shaped like q) is in token order.
+    return_indices=True also returns the routed key blocks, int32
+    [BH,nb,exact_blocks] ascending (diagnostics; sparse calls only)."""
     if q.ndim not in (3, 4) or q.shape != k.shape or q.shape != v.shape:
         raise ValueError("generic PISA requires matching [BH,T,D] or [B,H,T,D] q/k/v")
     if q.shape[-1] != HEAD_DIM:
@@ -337,7 +382,12 @@ def generic_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blo
     order = dict(order=_lib.ORDER_TILED8, grid=tuple(grid)) if grid is not None else {}
     views = [view(x, **order) for x in (q, k, v, out)]
     bh = q.shape[0] * (q.shape[1] if q.ndim == 4 else 1)
-    _native_forward(*views, q, bh, tokens, int(exact_blocks), _float32(scale), -2, _lib.STATS_GENERIC, first_order)
+    ws = _native_forward(*views, q, bh, tokens, int(exact_blocks), _float32(scale), -2, _lib.STATS_GENERIC,
+                         first_order)
+    if return_indices:
+        if not 0 < exact_blocks < blocks:
+            raise ValueError("routing is only produced by sparse calls.")
+        return out, _routing_from_workspace(ws, bh, tokens, int(exact_blocks))[0]
     return out
 
 
@@ -525,6 +575,7 @@ __all__ = [
     "fixed_block_attention",
     "forward",
     "forward_spatial_bhtd",
+    "forward_spatial_bhtd_with_routing",
     "full_attention",
     "generic_block_stats",
     "generic_forward",

@@ -26,6 +26,8 @@ B2_ERR_DEVICE = 4
 B2_BF16, B2_F16, B2_F32 = 0, 1, 2
 ORDER_LINEAR, ORDER_TILED8 = 0, 1
 STATS_HYD, STATS_GENERIC, STATS_SCALED = 0, 1, 2
+# workspace buffer indices of b2_pisa_workspace_layout (B2_WS_* in the header)
+WS_QC, WS_KC, WS_HSUM, WS_HNORM, WS_INDICES, WS_SEL, WS_FIELDS = 0, 1, 3, 5, 8, 9, 12
 
 _DTYPE_CODES = {torch.bfloat16: B2_BF16, torch.float16: B2_F16, torch.float32: B2_F32}
 
@@ -60,6 +62,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_last_kernel": (ctypes.c_char_p, []),
     "b2_read_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
     "b2_set_trace": (ctypes.c_int, [ctypes.c_void_p]),
+    "b2_debug_withhold_q": (ctypes.c_int, [_I32]),
     "b2_api_version": (ctypes.c_int, []),
     "b2_build_info": (ctypes.c_int, [ctypes.c_char_p, _I64]),
     "b2_check_device": (ctypes.c_int, [ctypes.c_int]),
@@ -69,6 +72,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_pisa_attention": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _F32, _VP, _VP]),
     "b2_pisa_pair": (ctypes.c_int, [_VP, _I32, _I32, _VP, _VP]),
     "b2_pisa_workspace_bytes": (_I64, [_I32, _I32, _I32, _I32]),
+    "b2_pisa_workspace_layout": (ctypes.c_int, [_I32, _I32, _I32, _I32, ctypes.POINTER(_I64), _I32]),
     "b2_pisa_forward": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _I32, _F32, _I32, _I32, _I32, _VP, _VP]),
     "b2_pisa_forward_spatial_host": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _I32, _I32, _I32,
                                                     _I32, _I32, _I32, _F32, _I32, _I32, _VP, _VP]),
@@ -163,3 +167,21 @@ def read_status() -> int:
     value = ctypes.c_int32(0)
     check(LIB.b2_read_status(ctypes.byref(value)))
     return value.value
+
+
+class PipelineTimeout(RuntimeError):
+    """A kernel's bounded pipeline wait ran out; its outputs are invalid."""
+
+    def __init__(self, status: int):
+        super().__init__(f"B200 attention pipeline wait timed out at site {status & 0xFF} "
+                         f"(status word 0x{status:x}); the launch's outputs are invalid")
+        self.status = status
+        self.site = status & 0xFF
+
+
+def check_status() -> None:
+    """Read and clear the device status word; raise PipelineTimeout when a
+    kernel since the last read gave up on a pipeline wait."""
+    status = read_status()
+    if status != 0:
+        raise PipelineTimeout(status)

@@ -383,13 +383,16 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     if (lane == 0 && !*abort_flag) {
       tma_prefetch_desc(&q_map);
       tma_prefetch_desc(&k_map);
-      mbar_expect_tx(&m.q_full, kQBytes);
-      for (int half = 0; half < 2; ++half)
-        for (int dh = 0; dh < 2; ++dh)
-          load_block(&q_map, a, q_s + dh * 16384 + half * 8192, &m.q_full, a.q_kind, bh, half ? qb : qa, dh);
+      if (!a.debug_withhold_q) {  // withheld only by the timeout diagnostics
+        mbar_expect_tx(&m.q_full, kQBytes);
+        for (int half = 0; half < 2; ++half)
+          for (int dh = 0; dh < 2; ++dh)
+            load_block(&q_map, a, q_s + dh * 16384 + half * 8192, &m.q_full, a.q_kind, bh, half ? qb : qa, dh);
+      }
       // key tiles 0..n-1, then the two 64-column halves of H as "tiles" n, n+1
       const int total = n + (a.has_corr ? 2 : 0);
-      for (int j = 0; j < total; ++j) {
+      int issued = 0;
+      for (int j = 0; j < total; ++j, issued = j) {
         const int s = j % kStagesK;
         if (!mbar_wait(&m.k_empty[s], ((j / kStagesK) & 1) ^ 1, abort_flag, a.status, 1)) break;
         char* slot = k_s + s * kSlotBytes;
@@ -407,12 +410,14 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           tma_load_3d(slot, &h_map, &m.k_full[s], (j - n) * 64, 0, bh);
         }
       }
+      if (*abort_flag) drain_loads(m.k_full, kStagesK, issued, a.debug_withhold_q ? nullptr : &m.q_full, a.status);
     }
   } else if (warp == Cfg<NW>::kVWarp) {
     // ------------------------------------------------------------ V producer
     if (lane == 0 && !*abort_flag) {
       tma_prefetch_desc(&v_map);
-      for (int j = 0; j < n; ++j) {
+      int issued = 0;
+      for (int j = 0; j < n; ++j, issued = j) {
         const int s = j % kStagesV;
         if (!mbar_wait(&m.v_empty[s], ((j / kStagesV) & 1) ^ 1, abort_flag, a.status, 13)) break;
         char* slot = v_s + s * kSlotBytes;
@@ -423,6 +428,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           else load_block(&v_map, a, slot + dh * 8192, &m.v_full[s], a.kv_kind, bh, t.blk, dh);
         }
       }
+      if (*abort_flag) drain_loads(m.v_full, kStagesV, issued, nullptr, a.status);
     }
   } else if (warp == 1 || (NW == 2 && warp == 11)) {
     // ------------------------------------------------------------ MMA issuers
@@ -867,6 +873,7 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   a.lse = p.lse;
   a.status = status;
   a.trace = p.trace;
+  a.debug_withhold_q = p.debug_withhold_q;
   a.pairs = p.mode == 1 ? p.pairs : nullptr;
   if (p.nb > 0) {
     const int last_len = kv.tokens - 64 * (p.nb - 1);

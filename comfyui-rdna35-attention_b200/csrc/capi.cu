@@ -46,6 +46,7 @@ namespace {
 thread_local char g_error[512] = "";
 thread_local const char* g_last_kernel = "none";
 long long* g_trace = nullptr;  // diagnostics timeline buffer (b2_set_trace)
+int g_withhold_q = 0;           // diagnostics: b2_debug_withhold_q
 
 // B200ATTN_KERNEL=mma forces the warp-level mma.sync attention kernel
 // (kept for layouts the TMA maps cannot express); default: tcgen05 kernel.
@@ -82,6 +83,7 @@ cudaError_t run_attention(const b2_view* q, const b2_view* k, const b2_view* v, 
   if (umma_enabled() && umma_supported(*q, *k, *v, *o)) {
     AttnParams pt = p;
     pt.trace = g_trace;
+    pt.debug_withhold_q = g_withhold_q;
     bool launched = false;
     int* status = device_status_ptr();
     if (status != nullptr) {
@@ -161,6 +163,7 @@ struct PisaWorkspace {
   int32_t* pairs;
   float* partial;
   size_t total;
+  size_t offset[B2_WS_FIELDS];  // byte offset of each buffer, in B2_WS_* order
 };
 
 PisaWorkspace carve(char* base, int bh, int tokens, int dim, int k) {
@@ -168,8 +171,10 @@ PisaWorkspace carve(char* base, int bh, int tokens, int dim, int k) {
   const int words = (nb + 31) / 32;
   PisaWorkspace w{};
   size_t off = 0;
+  int field = 0;
   auto take = [&](size_t bytes) {
     char* p = base ? base + off : nullptr;
+    w.offset[field++] = off;
     off += align256(bytes);
     return p;
   };
@@ -303,6 +308,11 @@ int b2_set_trace(long long* device_buffer) {
   return ok();
 }
 
+int b2_debug_withhold_q(int32_t enable) {
+  g_withhold_q = enable ? 1 : 0;
+  return ok();
+}
+
 int b2_read_status(int32_t* status) {
   if (status == nullptr) return fail(B2_ERR_INVALID, "status pointer is NULL");
   int* dev = device_status_ptr();
@@ -413,6 +423,16 @@ int b2_pisa_attention(const b2_view* q, const b2_view* k, const b2_view* v, cons
 int64_t b2_pisa_workspace_bytes(int32_t batch_heads, int32_t tokens, int32_t head_dim, int32_t exact_blocks) {
   if (batch_heads <= 0 || tokens <= 0 || head_dim != 128 || exact_blocks < 0) return -1;
   return static_cast<int64_t>(carve(nullptr, batch_heads, tokens, head_dim, exact_blocks).total);
+}
+
+int b2_pisa_workspace_layout(int32_t batch_heads, int32_t tokens, int32_t head_dim, int32_t exact_blocks,
+                             int64_t* offsets, int32_t n) {
+  if (batch_heads <= 0 || tokens <= 0 || head_dim != 128 || exact_blocks < 0)
+    return fail(B2_ERR_INVALID, "workspace layout needs BH, T > 0, D=128 and exact_blocks >= 0");
+  if (offsets == nullptr || n < 0) return fail(B2_ERR_INVALID, "offsets must be non-NULL");
+  const PisaWorkspace w = carve(nullptr, batch_heads, tokens, head_dim, exact_blocks);
+  for (int i = 0; i < n && i < B2_WS_FIELDS; ++i) offsets[i] = static_cast<int64_t>(w.offset[i]);
+  return ok();
 }
 
 int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, int32_t exact_blocks,

@@ -21,6 +21,7 @@ struct AttnParams {
   float* lse;
   int causal;
   long long* trace;
+  int debug_withhold_q;  // diagnostics: never load Q, so the pipeline's bounded waits run out
   const int32_t* pairs;  // optional [BH][ceil(nq/2)][2] query-block pairing (-1: single)
 };
 // Arguments of the tcgen05 attention kernel (see attn_umma.cu).
@@ -41,6 +42,7 @@ struct UmmaArgs {
   int* status;
   const int32_t* pairs;
   long long* trace;  // optional clock64 timeline of CTA (0,0): [tile][6] + start
+  int debug_withhold_q;  // diagnostics (b2_debug_withhold_q): Q is never loaded
 };
 bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const b2_view& o);
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,

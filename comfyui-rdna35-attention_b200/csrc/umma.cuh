@@ -89,6 +89,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// After an abort, wait (bounded by time only) until every TMA load this
+// producer issued into a ring of `stages` full-barriers has landed, so no bulk
+// copy still targets the CTA's shared memory when it exits.  `issued` loads
+// went to stages j % stages; `extra` (may be NULL) is one more barrier whose
+// phase 0 was armed.  Phases the consumers already saw complete at once.
+__device__ __forceinline__ void drain_loads(uint64_t* full, int stages, int issued, uint64_t* extra, int* status) {
+  int no_abort = 0;
+  for (int s = 0; s < stages && s < issued; ++s) {
+    const int last = s + ((issued - 1 - s) / stages) * stages;
+    mbar_wait(&full[s], (last / stages) & 1, &no_abort, status, 30);
+  }
+  if (extra != nullptr) mbar_wait(extra, 0, &no_abort, status, 31);
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -87,6 +87,14 @@ int b2_read_status(int32_t* status);
  * times of the four softmax warps + [256] S issue-return times, int64: 3073
  * entries; see attn_umma.cu).  NULL disables. */
 int b2_set_trace(long long* device_buffer);
+/* Diagnostics (no counterpart in the reference): while enabled, later
+ * tcgen05 attention launches of this process never load their Q tile, so
+ * their pipelines stall on a barrier that nothing completes.  Every wait of
+ * the kernel is bounded (about 2^31 cycles): the CTAs then record
+ * (1 << 8 | site) in the status word, wait for their own loads in flight,
+ * free TMEM and return, leaving the context usable.  Used by the tests of
+ * that timeout path; outputs of such launches are invalid. */
+int b2_debug_withhold_q(int32_t enable);
 int b2_api_version(void);
 /* Writes a NUL-terminated "key=value;..." build description. */
 int b2_build_info(char* buffer, int64_t capacity);
@@ -184,6 +192,27 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v,
                     const b2_view* out, int32_t exact_blocks, float scale,
                     int32_t sink_block, int32_t stats_mode,
                     int32_t first_order, void* workspace, void* stream);
+
+/* ---- Byte offsets of the buffers b2_pisa_forward carves out of its
+ * workspace, so a caller can read the routing it used (no counterpart in the
+ * reference, whose forward keeps its indices internal;
+ * rdna35_pisa_ck/__init__.py:262-264 computes them).  Writes up to n offsets,
+ * indexed by the B2_WS_* constants below, and returns 0, or B2_ERR_INVALID
+ * for sizes b2_pisa_workspace_bytes rejects.  After a sparse b2_pisa_forward
+ * (0 < exact_blocks < nb) on `stream` completes:
+ *   B2_WS_INDICES  int32  [BH,nb,exact_blocks] routed key blocks, ascending;
+ *   B2_WS_SEL      uint32 [BH,nb,ceil(nb/32)] the same sets as bitsets;
+ *   B2_WS_HNORM    FP32   [BH,nb] HYD covariance norms;
+ *   B2_WS_QC/KC    query (BF16 HYD / FP32 generic) and FP32 key centroids
+ *                  [BH,nb,D]; B2_WS_HSUM FP32 [BH,D,D]. */
+enum {
+  B2_WS_QC = 0, B2_WS_KC = 1, B2_WS_VSTAT = 2, B2_WS_HSUM = 3, B2_WS_H16 = 4,
+  B2_WS_HNORM = 5, B2_WS_KC16 = 6, B2_WS_VC16 = 7, B2_WS_INDICES = 8,
+  B2_WS_SEL = 9, B2_WS_PAIRS = 10, B2_WS_PARTIAL = 11, B2_WS_FIELDS = 12
+};
+int b2_pisa_workspace_layout(int32_t batch_heads, int32_t tokens,
+                             int32_t head_dim, int32_t exact_blocks,
+                             int64_t* offsets, int32_t n);
 
 /* ---- Pipelined PISA HYD forward from host memory.  No counterpart in the
  * reference (its forward_spatial_bhtd, rdna35_pisa_ck/__init__.py:406-433,

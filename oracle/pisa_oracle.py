@@ -155,14 +155,16 @@ def select_topk(scores: torch.Tensor, exact_blocks: int, sink_block: int | None 
     return order[..., :exact_blocks].sort(dim=-1).values
 
 
-def near_tie_rows(scores: torch.Tensor, exact_blocks: int, rel: float = 1e-5) -> torch.Tensor:
-    """Rows whose k-th and (k+1)-th largest scores lie within rel*max(1,|s|):
-    index sets there may legitimately differ between implementations."""
+def near_tie_rows(scores: torch.Tensor, exact_blocks: int, rel: float = 1e-5, abs_tol: float = 0.0) -> torch.Tensor:
+    """Rows whose k-th and (k+1)-th largest scores lie within
+    rel*max(1,|s|) + abs_tol: index sets there may legitimately differ between
+    implementations.  abs_tol carries a bound on the per-column score error
+    of the implementation under test (e.g. twice its max |d log h_norm|)."""
     if exact_blocks <= 0 or exact_blocks >= scores.shape[-1]:
         return torch.zeros(scores.shape[:-1], dtype=torch.bool)
     top = torch.topk(scores, exact_blocks + 1, dim=-1).values
     a, b = top[..., exact_blocks - 1], top[..., exact_blocks]
-    return (a - b).abs() <= rel * torch.clamp(a.abs(), min=1.0)
+    return (a - b).abs() <= rel * torch.clamp(a.abs(), min=1.0) + abs_tol
 
 
 # ----------------------------------------------------------------- attention
@@ -226,6 +228,85 @@ def hyd_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks:
     return out.to(q.dtype), indices
 
 
+def _blocked_sparse_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                            tail_keys: torch.Tensor, tail_values: torch.Tensor, tail_bias: torch.Tensor,
+                            correction: torch.Tensor | None, scale: float, chunk: int = 32) -> torch.Tensor:
+    """Batched form of the per-query-block loops of hyd_forward /
+    generic_forward for one (batch, head): the selected key rows of every
+    query block are gathered at once (chunks of ``chunk`` query blocks) and
+    the exact, tail and correction terms are merged with LSE weights exactly
+    as those loops do (exact and tail outputs rounded to q.dtype first).
+    q/k/v: [T,D]; indices [nb,kx]; tail_keys [nb,D] (already rounded);
+    tail_values [nb,D] FP32; tail_bias [nb] added to every tail logit;
+    correction [T,D] FP32 or None.  Returns FP32 [T,D]."""
+    tokens, d = q.shape
+    nb = indices.shape[0]
+    kx = indices.shape[1]
+    pad = nb * BLOCK_SIZE - tokens
+    qf = F.pad(q.float(), (0, 0, 0, pad)).view(nb, BLOCK_SIZE, d)
+    kf = F.pad(k.float(), (0, 0, 0, pad))
+    vf = F.pad(v.float(), (0, 0, 0, pad))
+    out = torch.empty((nb, BLOCK_SIZE, d), dtype=torch.float32)
+    sel_mask = torch.zeros((nb, nb), dtype=torch.bool)
+    if kx:
+        sel_mask.scatter_(1, indices.long(), True)
+    lane = torch.arange(BLOCK_SIZE)
+    corr = None if correction is None else F.pad(correction, (0, 0, 0, pad)).view(nb, BLOCK_SIZE, d)
+    for c0 in range(0, nb, chunk):
+        c1 = min(nb, c0 + chunk)
+        qb = qf[c0:c1]
+        tail = torch.matmul(qb, tail_keys.T) * scale + tail_bias[None, None]
+        tail = tail.masked_fill(sel_mask[c0:c1, None, :], -torch.inf)
+        tail_lse = torch.logsumexp(tail, -1)
+        tail_out = torch.matmul(torch.exp(tail - tail_lse[..., None]), tail_values).to(q.dtype).float()
+        wa_corr = corr[c0:c1] if corr is not None else None
+        if kx == 0:
+            o = tail_out if wa_corr is None else tail_out + wa_corr
+        else:
+            rows = (indices[c0:c1].long()[..., None] * BLOCK_SIZE + lane).reshape(c1 - c0, kx * BLOCK_SIZE)
+            s = torch.bmm(qb, kf[rows].transpose(1, 2)) * scale
+            s = s.masked_fill((rows >= tokens)[:, None, :], -torch.inf)
+            ex_lse = torch.logsumexp(s, -1)
+            ex_out = torch.bmm(torch.exp(s - ex_lse[..., None]), vf[rows]).to(q.dtype).float()
+            total = torch.logaddexp(ex_lse, tail_lse)
+            we = torch.exp(ex_lse - total)[..., None]
+            wa = torch.exp(tail_lse - total)[..., None]
+            o = ex_out * we + tail_out * wa
+            if wa_corr is not None:
+                o = o + wa_corr * wa
+        out[c0:c1] = o
+    return out.view(nb * BLOCK_SIZE, d)[:tokens]
+
+
+def hyd_forward_batched(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int,
+                        scale: float | None = None, sink_block: int | None = None, stats=None, heads=None):
+    """hyd_forward with the per-query-block loop replaced by gathered batched
+    matmuls (the shape of the reference's own torch ops,
+    rdna35_pisa_ck/__init__.py:254-316).  Same semantics and return value;
+    ``heads`` restricts the attention to those rows of the [BH,...] inputs
+    (their outputs only; other rows of the result are left zero)."""
+    bh, tokens, d = q.shape
+    nb = (tokens + BLOCK_SIZE - 1) // BLOCK_SIZE
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    scale = float(torch.tensor(scale, dtype=torch.float32))
+    if exact_blocks == nb:
+        out, _ = _softmax_attend(q, k, v, scale)
+        return out.to(q.dtype), torch.arange(nb).expand(bh, nb, nb)
+    qc, kc, vc, h_sum, h_norm = stats if stats is not None else hyd_block_stats(q, k, v)
+    if exact_blocks > 0:
+        indices = select_topk(route_scores_hyd(qc, kc, h_norm, scale), exact_blocks, sink_block)
+    else:
+        indices = torch.empty((bh, nb, 0), dtype=torch.int64)
+    log_lens = torch.tensor(block_lengths(tokens), dtype=torch.float32).log()
+    kcb = kc.to(q.dtype).float()
+    out = torch.zeros((bh, tokens, d), dtype=torch.float32)
+    corr_scale = torch.tensor(scale / tokens, dtype=torch.float32)
+    for b in (range(bh) if heads is None else heads):
+        corr = torch.matmul(q[b].float(), h_sum[b].to(q.dtype).float()) * corr_scale
+        out[b] = _blocked_sparse_forward(q[b], k[b], v[b], indices[b], kcb[b], vc[b].float(), log_lens, corr, scale)
+    return out.to(q.dtype), indices
+
+
 def hyd_forward_spatial(q_bhtd: torch.Tensor, k_bhtd: torch.Tensor, v_bhtd: torch.Tensor, exact_blocks: int,
                         scale: float | None = None, sink_block: int | None = None):
     """forward_spatial_bhtd (rdna35_pisa_ck/__init__.py:344-365): pack, HYD
@@ -275,6 +356,29 @@ def generic_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blo
             if corr_all is not None:
                 o = o + corr_all[b, s0:s1] * wa
             out[b, s0:s1] = o
+    return out.to(q.dtype), indices
+
+
+def generic_forward_batched(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int,
+                            scale: float | None = None, use_first_order: bool = True, heads=None):
+    """generic_forward with gathered batched matmuls in place of its
+    per-query-block loop; same semantics.  ``heads`` as in hyd_forward_batched."""
+    bh, tokens, d = q.shape
+    nb = (tokens + BLOCK_SIZE - 1) // BLOCK_SIZE
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    if exact_blocks == nb:
+        out, _ = _softmax_attend(q, k, v, scale)
+        return out.to(q.dtype), torch.arange(nb).expand(bh, nb, nb)
+    qc, kc, vsum, h_sum, lens = generic_block_stats(q, k, v)
+    vmean = vsum / lens[None, :, None]
+    indices = select_topk(route_scores_generic(qc, kc, scale), exact_blocks)
+    kcb = kc.to(q.dtype).float()
+    out = torch.zeros((bh, tokens, d), dtype=torch.float32)
+    for b in (range(bh) if heads is None else heads):
+        corr = None
+        if use_first_order:
+            corr = torch.matmul(q[b].float(), h_sum[b].to(q.dtype).float()) * (scale / tokens)
+        out[b] = _blocked_sparse_forward(q[b], k[b], v[b], indices[b], kcb[b], vmean[b], lens.log(), corr, scale)
     return out.to(q.dtype), indices
 
 

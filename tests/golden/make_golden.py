@@ -9,7 +9,8 @@ package -- and writes tests/golden/golden.pt:
   * pisa_hyd: _pisa_reference of native/rdna35_pisa_ck/tests/test_forward.py
     (the reference's own pure-torch HYD oracle; the native wheel it imports
     is stubbed because it cannot load without its ROCm build) for T in
-    {65, 128, 256} with exact_blocks 0/1/2 and sink blocks;
+    {65, 128, 256} with exact_blocks 0/1/2 and sink blocks, and at the full
+    Anima size T=9216 with 23 of 144 exact blocks (every 8th output row);
   * pisa_paper: pisa_attention(backend="reference") (paper variant);
   * h3_pack: pack_minimax_h3_qkv value/identity checks;
   * tiling: generic_pisa._pack_spatial_blocks / _pack_video_blocks
@@ -31,6 +32,15 @@ def seeded(shape, seed, dtype=torch.float32):
     return torch.randn(shape, generator=gen).to(dtype)
 
 
+def block_offset_inputs(tokens, seed, dtype=torch.bfloat16):
+    """[1,T,128] N(0,1) plus a per-64-token-block N(0,0.5) offset (config 3's
+    value distribution in block-major order)."""
+    blocks = (tokens + 63) // 64
+    base = seeded((1, blocks * 64, 128), seed)
+    off = seeded((1, blocks, 1, 128), seed + 100000) * 0.5
+    return (base.view(1, blocks, 64, 128) + off).view(1, blocks * 64, 128)[:, :tokens].contiguous().to(dtype)
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     sys.modules["rdna35_pisa_ck"] = types.ModuleType("rdna35_pisa_ck")  # stub: ROCm-only wheel
@@ -45,7 +55,7 @@ def main(ref_root: str) -> None:
     spec.loader.exec_module(test_forward)
     pisa_reference = test_forward._pisa_reference
 
-    golden: dict = {"fixed_block": [], "pisa_hyd": [], "pisa_paper": [], "tiling": {}, "h3_pack": {}}
+    golden: dict = {"fixed_block": [], "pisa_hyd": [], "pisa_hyd_full": [], "pisa_paper": [], "tiling": {}, "h3_pack": {}}
     for causal in (False, True):
         q, k, v = (seeded((1, 2, 256, 64), 100 + i) for i in range(3))
         out = fixed_block_attention_ref(q, k, v, block_size=64, scale=0.125, causal=causal, layout="bhtd")
@@ -57,6 +67,14 @@ def main(ref_root: str) -> None:
         out = pisa_reference(q, k, v, exact_blocks=exact, sink_block=sink)
         golden["pisa_hyd"].append({"seeds": tuple(seed * 10 + i for i in range(3)), "tokens": tokens,
                                    "exact_blocks": exact, "sink_block": sink, "out": out.to(torch.bfloat16)})
+    # full Anima block count (144 blocks, the 23-block cut) on block-offset
+    # inputs so the routing is non-trivial; every 8th output row is stored
+    for tokens, exact, sink, seed in ((9216, 23, None, 71), (9216, 23, 0, 73)):
+        q, k, v = (block_offset_inputs(tokens, seed * 10 + i) for i in range(3))
+        out = pisa_reference(q, k, v, exact_blocks=exact, sink_block=sink)
+        golden["pisa_hyd_full"].append({"seeds": tuple(seed * 10 + i for i in range(3)), "tokens": tokens,
+                                        "exact_blocks": exact, "sink_block": sink, "row_step": 8,
+                                        "out_rows": out[:, ::8].to(torch.bfloat16).clone()})
     for tokens, exact, seed in ((256, 2, 41), (200, 1, 43)):
         q, k, v = (seeded((2, tokens, 128), seed * 10 + i, torch.bfloat16) for i in range(3))
         out = pisa_attention(q, k, v, exact_blocks=exact, backend="reference")

@@ -81,3 +81,25 @@ def test_selection_ties_resolve_to_lower_index():
     scores = torch.tensor([[[1.0, 3.0, 3.0, 2.0, 3.0]]])
     assert oracle.select_topk(scores, 2).tolist() == [[[1, 2]]]
     assert oracle.select_topk(scores, 2, sink_block=0).tolist() == [[[0, 1]]]
+
+
+def block_offset_inputs(tokens, seed, dtype=torch.bfloat16):
+    blocks = (tokens + 63) // 64
+    base = seeded((1, blocks * 64, 128), seed)
+    off = seeded((1, blocks, 1, 128), seed + 100000) * 0.5
+    return (base.view(1, blocks, 64, 128) + off).view(1, blocks * 64, 128)[:, :tokens].contiguous().to(dtype)
+
+
+@pytest.mark.parametrize("case", GOLDEN["pisa_hyd_full"], ids=lambda c: f"T{c['tokens']}_k{c['exact_blocks']}_s{c['sink_block']}")
+def test_hyd_oracle_matches_reference_at_full_anima_size(case):
+    # 144 blocks with the 23-block cut: the loop oracle and its batched form
+    # (the CPU baseline) both agree with the reference's _pisa_reference at
+    # its own 5e-2 gate, and with each other exactly
+    q, k, v = (block_offset_inputs(case["tokens"], s) for s in case["seeds"])
+    stats = oracle.hyd_block_stats(q, k, v)
+    batched, idx_b = oracle.hyd_forward_batched(q, k, v, case["exact_blocks"], sink_block=case["sink_block"], stats=stats)
+    rows = batched[:, ::case["row_step"]]
+    torch.testing.assert_close(rows.float(), case["out_rows"].float(), atol=5e-2, rtol=5e-2)
+    loop, idx_l = oracle.hyd_forward(q, k, v, case["exact_blocks"], sink_block=case["sink_block"], stats=stats)
+    assert torch.equal(idx_b, idx_l)
+    torch.testing.assert_close(batched.float(), loop.float(), atol=1e-2, rtol=1e-2)  # matmul blocking order
