@@ -6,19 +6,26 @@ storage, 23 of 144 exact KV blocks per query block.  One step = one
 ``b200_pisa.forward_spatial_bhtd`` call over the whole batch (statistics,
 routing, fused exact + tail + correction attention, raster output).
 
-Multi-GPU (torchrun, one process per GPU): weak scaling -- every rank runs the
-full config-3 call on its own (batch, head) set; no collective on the data
-path.  Timing: W untimed warm-ups, then K steps between a barrier +
-synchronize on both sides, CUDA events on the launching stream, max over
-ranks.  The inputs (226 MB of q/k/v) exceed the 126 MB L2, so no extra flush.
+Multi-GPU (torchrun, one process per GPU): strong scaling of the same call --
+the 16 heads are split into N equal contiguous ranges
+(``b200_pisa.sharded.head_range``); each rank holds its heads' q/k/v
+([B,T,H/N,D] raster), computes them with the single-GPU kernels and one NCCL
+all-gather plus an interleave kernel assemble the full [B,T,H*D] output on
+every rank (``forward_spatial_bhtd_sharded``).  Timing: W untimed warm-ups,
+then K steps between a barrier + synchronize on both sides, CUDA events on
+the launching stream, max over ranks.  The inputs (226 MB of q/k/v) exceed
+the 126 MB L2, so no extra flush.
 
-``e2e`` is the same call for activations in pinned host memory
-(``b200_pisa.forward_spatial_bhtd_host``: the copies in and out are inside
-the timed region and overlap the compute of neighbouring head stages); the
-unstaged copy-in, call, copy-out time is reported beside it.
+``e2e`` is the same call for activations in pinned host memory.  On one GPU
+it is ``b200_pisa.forward_spatial_bhtd_host`` (the copies in and out are
+inside the timed region and overlap the compute of neighbouring head
+stages; the unstaged copy-in, call, copy-out time is reported beside it).
+On N GPUs each rank copies its heads' q/k/v in, runs the sharded call and
+copies the full gathered output out.
 
 ``--impl reference`` times the reference's PyTorch HYD path restated on the
-host CPU (oracle/pisa_oracle.py) on a bounded sample and reports the same
+host CPU (oracle/pisa_oracle.py, the batched form that mirrors the
+reference's torch ops) for the whole 32-head call and reports the same
 metric.
 
 ``--workload`` selects one of the other configs instead of the headline one
@@ -56,8 +63,8 @@ EXACT_FLOP = 4.0 * B * H * NB * EXACT * 64 * 64 * D       # 222.3 GFLOP
 TAIL_FLOP = 4.0 * B * H * T * NB * D                      # 21.7 GFLOP (q.kc and p.vc)
 CORR_FLOP = 2.0 * B * H * T * D * D                       # 9.66 GFLOP
 STATS_BYTES = 3 * B * H * T * D * 2                       # q/k/v read once
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture
-# of this workload (profiles/attn_umma_anima.md, profiles/stats_umma_anima.md)
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu
+# capture of this workload's attention and statistics kernels
 ATTN_TRAFFIC = 290.8e6
 STATS_TRAFFIC = 241.7e6
 CONFIG = {
@@ -97,9 +104,11 @@ def max_over_ranks(x: float, device) -> float:
 
 
 def job_value(world: int, ms: float) -> float:
-    """Whole-job dense-equivalent TFLOP/s: every rank runs one full call
-    (weak scaling), the job takes the slowest rank's time."""
-    return world * DENSE_FLOP / (ms * 1e-3) / 1e12
+    """Whole-job dense-equivalent TFLOP/s: the N ranks together run one
+    config-3 call (strong scaling: heads split over the ranks, outputs
+    gathered), which takes the slowest rank's time."""
+    del world  # the call's work does not grow with the number of ranks
+    return DENSE_FLOP / (ms * 1e-3) / 1e12
 
 
 class ClockSampler:
@@ -206,17 +215,24 @@ def run_b200(args) -> None:
     sys.path.insert(0, str(ROOT / "oracle"))
     import b200_pisa
     from b200_pisa import _lib
+    from b200_pisa.sharded import forward_spatial_bhtd_sharded, gather_head_shards, head_range
 
     b200_pisa.prepare(local)
-    q_cpu, k_cpu, v_cpu = _inputs(device, seed=rank)
-    # raster BTHD storage on the host (pinned), BHTD views on the device
-    host = [x.permute(0, 2, 1, 3).contiguous().pin_memory() for x in (q_cpu, k_cpu, v_cpu)]
+    h0, h1 = head_range(H, world, rank)
+    hs = h1 - h0
+    q_cpu, k_cpu, v_cpu = _inputs(device, seed=0)  # the same call on every rank
+    # this rank's heads as raster BTHD storage on the host (pinned), BHTD views on the device
+    host = [x[:, h0:h1].permute(0, 2, 1, 3).contiguous().pin_memory() for x in (q_cpu, k_cpu, v_cpu)]
+    del q_cpu, k_cpu, v_cpu
     dev = [h.to(device).permute(0, 2, 1, 3) for h in host]
     q, k, v = dev
     stream = torch.cuda.current_stream(device)
+    out_dev = torch.empty((B, T, H * D), device=device, dtype=torch.bfloat16)
 
     def step():
-        return b200_pisa.forward_spatial_bhtd(q, k, v, exact_blocks=EXACT)
+        if world == 1:
+            return b200_pisa.forward_spatial_bhtd(q, k, v, exact_blocks=EXACT)
+        return forward_spatial_bhtd_sharded(q, k, v, EXACT, out=out_dev)
 
     for _ in range(args.warmup):
         step()
@@ -243,17 +259,35 @@ def run_b200(args) -> None:
     clock_info = clocks.summary()
     ms = max_over_ranks(ms, device)
     value = job_value(world, ms)
+    gather_ms = None
+    if world > 1:
+        # the exchange alone: all-gather of this rank's [B,T,Hs*D] + interleave
+        local_out = b200_pisa.forward_spatial_bhtd(q, k, v, exact_blocks=EXACT)
+        barrier()
+        gather_ms = max_over_ranks(_timed(lambda: gather_head_shards(local_out, out=out_dev), args.steps, stream),
+                                   device)
+        barrier()
 
-    # ---- end to end through the public API for host-resident activations:
-    # pinned host q/k/v in, pinned host output out, all inside the timed
-    # region; forward_spatial_bhtd_host stages the call by heads so the PCIe
-    # copies overlap the compute of neighbouring stages
+    # ---- end to end through the public API for host-resident activations
     out_host = torch.empty((B, T, H * D), dtype=torch.bfloat16).pin_memory()
     host_bhtd = [h.permute(0, 2, 1, 3) for h in host]
+    serial_ms = None
+    if world == 1:
+        # pinned host q/k/v in, pinned host output out, all inside the timed
+        # region; forward_spatial_bhtd_host stages the call by heads so the
+        # PCIe copies overlap the compute of neighbouring stages
+        def e2e_step():
+            b200_pisa.forward_spatial_bhtd_host(*host_bhtd, exact_blocks=EXACT, device=device, out=out_host,
+                                                heads_per_stage=args.heads_per_stage)
+    else:
+        # this rank's heads in, sharded call with the all-gather, full output out
+        dev_bthd = [torch.empty_like(h, device=device) for h in host]
 
-    def e2e_step():
-        b200_pisa.forward_spatial_bhtd_host(*host_bhtd, exact_blocks=EXACT, device=device, out=out_host,
-                                            heads_per_stage=args.heads_per_stage)
+        def e2e_step():
+            for d_, h_ in zip(dev_bthd, host):
+                d_.copy_(h_, non_blocking=True)
+            out = forward_spatial_bhtd_sharded(*(x.permute(0, 2, 1, 3) for x in dev_bthd), EXACT, out=out_dev)
+            out_host.copy_(out, non_blocking=True)
 
     for _ in range(2):
         e2e_step()
@@ -262,57 +296,63 @@ def run_b200(args) -> None:
     barrier()
     e2e_ms = max_over_ranks(e2e_ms, device)
 
-    # the same end-to-end call without staging (copy all in, call, copy out)
-    dev_bthd = [torch.empty_like(h, device=device) for h in host]
+    if world == 1:
+        # the same end-to-end call without staging (copy all in, call, copy out)
+        dev_bthd = [torch.empty_like(h, device=device) for h in host]
 
-    def serial_step():
-        for d_, h_ in zip(dev_bthd, host):
-            d_.copy_(h_, non_blocking=True)
-        out = b200_pisa.forward_spatial_bhtd(*(x.permute(0, 2, 1, 3) for x in dev_bthd), exact_blocks=EXACT)
-        out_host.copy_(out, non_blocking=True)
+        def serial_step():
+            for d_, h_ in zip(dev_bthd, host):
+                d_.copy_(h_, non_blocking=True)
+            out = b200_pisa.forward_spatial_bhtd(*(x.permute(0, 2, 1, 3) for x in dev_bthd), exact_blocks=EXACT)
+            out_host.copy_(out, non_blocking=True)
 
-    serial_step()
-    barrier()
-    serial_ms = max_over_ranks(_timed(serial_step, max(2, args.steps // 4), stream), device)
-    barrier()
-    del dev_bthd
+        serial_step()
+        barrier()
+        serial_ms = max_over_ranks(_timed(serial_step, max(2, args.steps // 4), stream), device)
+        barrier()
+        del dev_bthd
     h2d = sum(h.numel() * h.element_size() for h in host)
     d2h = out_host.numel() * out_host.element_size()
 
-    # ---- component timing (dominant kernels, separate entry points)
+    # ---- component timing (dominant kernels, separate entry points, this rank's heads)
     comp = component_times(b200_pisa, _lib, q, k, v, device, stream, args.steps)
 
     peaks = _peaks()
-    attn_flop = EXACT_FLOP + TAIL_FLOP + CORR_FLOP
+    share = hs / H
+    attn_flop = (EXACT_FLOP + TAIL_FLOP + CORR_FLOP) * share
     achieved = attn_flop / (comp["attention_ms"] * 1e-3) / 1e12
+    stats_gbs = STATS_BYTES * share / (comp["stats_ms"] * 1e-3) / 1e9
     roofline = {
         "kernel": "attn_kernel (fused exact + tail + correction)",
         "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16"], "unit": "TFLOP/s",
         "frac": round(achieved / peaks["bf16"], 4), "peak_source": peaks["source"] + " bf16 burst",
-        "traffic": args.traffic if args.traffic is not None else ATTN_TRAFFIC,
+        "traffic": (args.traffic if args.traffic is not None else ATTN_TRAFFIC) * share,
         "stats_kernel": {
-            "bound": "hbm", "achieved": round(STATS_BYTES / (comp["stats_ms"] * 1e-3) / 1e9, 1),
-            "peak": peaks["hbm"], "unit": "GB/s",
-            "frac": round(STATS_BYTES / (comp["stats_ms"] * 1e-3) / 1e9 / peaks["hbm"], 4),
-            "traffic": STATS_TRAFFIC,
+            "bound": "hbm", "achieved": round(stats_gbs, 1), "peak": peaks["hbm"], "unit": "GB/s",
+            "frac": round(stats_gbs / peaks["hbm"], 4), "traffic": STATS_TRAFFIC * share,
         },
         "component_ms": comp,
     }
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) + per-tile N(0,0.5) offsets)",
-            "config": CONFIG, "clocks": clock_info,
+            "config": {**CONFIG, "parallelism": f"heads split over {world} GPU(s), {hs} per rank"
+                       + (", NCCL all-gather of the outputs" if world > 1 else "")},
+            "clocks": clock_info,
             "e2e": {"value": round(job_value(world, e2e_ms), 2), "unit": UNIT,
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "forward_spatial_bhtd_host", "heads_per_stage": args.heads_per_stage,
-                    "unstaged_ms_per_step": round(serial_ms, 4)},
-            "gpu_launches": 6 * args.steps,
+                    "api": "forward_spatial_bhtd_host" if world == 1 else "forward_spatial_bhtd_sharded",
+                    **({"heads_per_stage": args.heads_per_stage, "unstaged_ms_per_step": round(serial_ms, 4)}
+                       if world == 1 else {})},
+            "gpu_launches": (6 + (1 if world > 1 else 0)) * args.steps,
             "roofline": roofline,
         }
+        if gather_ms is not None:
+            line["gather_ms"] = round(gather_ms, 4)
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(args.cpu_heads)
+            line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line))
     if world > 1:
         import torch.distributed as dist
@@ -327,11 +367,12 @@ def component_times(b200_pisa, _lib, q, k, v, device, stream, steps):
 
     from b200_pisa import LIB, check
 
-    bh = B * H
+    heads = q.shape[1]
+    bh = B * heads
     grid = dict(order=_lib.ORDER_TILED8, grid=(96, 96))
     qv, kv, vv = (_lib.view(x, **grid) for x in (q, k, v))
-    out = torch.empty((B, T, H * D), device=device, dtype=torch.bfloat16)
-    ov = _lib.view(out.view(B, T, H, D).permute(0, 2, 1, 3), **grid)
+    out = torch.empty((B, T, heads * D), device=device, dtype=torch.bfloat16)
+    ov = _lib.view(out.view(B, T, heads, D).permute(0, 2, 1, 3), **grid)
     qc = torch.empty((bh, NB, D), device=device, dtype=torch.bfloat16)
     kc = torch.empty((bh, NB, D), device=device, dtype=torch.float32)
     vc = torch.empty((bh, NB, D), device=device, dtype=torch.bfloat16)
@@ -383,23 +424,29 @@ def component_times(b200_pisa, _lib, q, k, v, device, stream, steps):
     return out
 
 
-def cpu_baseline(heads: int) -> dict:
-    """The oracle (restated reference PyTorch HYD path) on host cores, on a
-    bounded sample of `heads` (batch, head) pairs at full T, scaled to the
-    metric for the full 32-head call."""
-    sys.path.insert(0, str(ROOT / "oracle"))
+def _oracle_call(q, k, v):
+    """The reference's HYD path restated on the host (oracle/pisa_oracle.py,
+    batched form of rdna35_pisa_ck/__init__.py:254-316): pack, statistics,
+    routing, gathered exact + tail + correction, raster output."""
     import pisa_oracle
 
+    packed = [pisa_oracle.pack_spatial(x) for x in (q, k, v)]
+    out, _ = pisa_oracle.hyd_forward_batched(*packed, EXACT)
+    return pisa_oracle.unpack_spatial(out, q.shape[0], q.shape[1])
+
+
+def cpu_baseline() -> dict:
+    """The oracle on all host cores, one full 32-head call (a few seconds)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    q, k, v = pisa_oracle.anima_inputs(batch=1, heads=heads, seed=0)
+    q, k, v = _inputs(None, seed=0)
     t0 = time.perf_counter()
-    pisa_oracle.hyd_forward_spatial(q, k, v, EXACT)
+    _oracle_call(q, k, v)
     sec = time.perf_counter() - t0
-    call_sec = sec * (B * H) / heads
-    return {"value": round(DENSE_FLOP / call_sec / 1e12, 5), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{heads} of {B * H} (batch, head) pairs at T=9216, scaled x{B * H // heads}",
-            "ms_per_call_extrapolated": round(call_sec * 1e3, 1)}
+    return {"value": round(DENSE_FLOP / sec / 1e12, 5), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"one full call, all {B * H} (batch, head) pairs at T=9216 (no extrapolation)",
+            "ms_per_call": round(sec * 1e3, 1)}
 
 
 def run_reference(args) -> None:
@@ -407,26 +454,23 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     sys.path.insert(0, str(ROOT / "oracle"))
-    import pisa_oracle
-
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    heads = args.cpu_heads
-    q, k, v = pisa_oracle.anima_inputs(batch=1, heads=heads, seed=0)
+    q, k, v = _inputs(None, seed=0)
     for _ in range(args.warmup):
-        pisa_oracle.hyd_forward_spatial(q, k, v, EXACT)
+        _oracle_call(q, k, v)
     samples = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        pisa_oracle.hyd_forward_spatial(q, k, v, EXACT)
+        _oracle_call(q, k, v)
         samples.append(time.perf_counter() - t0)
-    call_ms = statistics.median(samples) * 1e3 * (B * H) / heads
+    call_ms = statistics.median(samples) * 1e3
     value = DENSE_FLOP / (call_ms * 1e-3) / 1e12
-    sample = f"{heads} of {B * H} (batch, head) pairs at T=9216 per step, scaled x{B * H // heads}"
+    sample = f"one full call per step, all {B * H} (batch, head) pairs at T=9216 (no extrapolation)"
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(call_ms, 2), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": CONFIG,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": CONFIG,
         "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
@@ -933,7 +977,6 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    parser.add_argument("--cpu-heads", type=int, default=1)
     parser.add_argument("--heads-per-stage", type=int, default=4,
                         help="heads per copy/compute stage of the end-to-end (host memory) call")
     parser.add_argument("--workload", default="anima", choices=["anima", *WORKLOADS],

@@ -1,9 +1,10 @@
 """Multi-process host logic of bench.py on CPU: two gloo ranks.
 
-bench.py runs one process per GPU (weak scaling, no collective on the data
-path); the only cross-rank steps are the max over ranks of the timed
-region and rank-0-only output.  Those run here with the gloo backend on
-127.0.0.1, without a GPU.
+bench.py runs one process per GPU (strong scaling: the heads of one call
+are split over the ranks and the outputs all-gathered); the host-side
+cross-rank steps are the max over ranks of the timed region, the job value
+and rank-0-only output.  Those run here with the gloo backend on
+127.0.0.1, without a GPU (the head exchange itself: test_host_sharded.py).
 """
 import io
 import os
@@ -40,7 +41,7 @@ def _worker(rank, world, port, results):
         # the reference arm runs on rank 0 only; other ranks print nothing
         buf = io.StringIO()
         if rank != 0:
-            args = type("A", (), {"cpu_heads": 1, "warmup": 0, "steps": 0})()
+            args = type("A", (), {"warmup": 0, "steps": 0})()
             with redirect_stdout(buf):
                 bench.run_reference(args)
         results[rank] = (w, r, local, slowest, value, buf.getvalue())
@@ -59,7 +60,8 @@ def test_two_gloo_ranks_take_the_slowest_time():
         w, r, local, slowest, value, out = results[rank]
         assert (w, r, local) == (world, rank, rank)
         assert slowest == 2.0  # max over ranks, seen identically by every rank
-        assert abs(value - world * bench.DENSE_FLOP / 2e-3 / 1e12) < 1e-9
+        # strong scaling: the ranks share one call, timed by the slowest rank
+        assert abs(value - bench.DENSE_FLOP / 2e-3 / 1e12) < 1e-9
         assert out == ""
 
 
