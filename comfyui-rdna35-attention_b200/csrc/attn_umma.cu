@@ -230,7 +230,9 @@ __device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, con
   return true;
 }
 
-template <bool BF16, int NW>
+// WITHHOLD (the timeout diagnostics of b2_debug_withhold_q only): the Q tile
+// is never loaded, so the pipeline's bounded waits run out.
+template <bool BF16, int NW, bool WITHHOLD>
 __global__ void __launch_bounds__(Cfg<NW>::kThreads, Cfg<NW>::kCtasPerSm)
 attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                  const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap kc_map,
@@ -383,7 +385,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     if (lane == 0 && !*abort_flag) {
       tma_prefetch_desc(&q_map);
       tma_prefetch_desc(&k_map);
-      if (!a.debug_withhold_q) {  // withheld only by the timeout diagnostics
+      if constexpr (!WITHHOLD) {
         mbar_expect_tx(&m.q_full, kQBytes);
         for (int half = 0; half < 2; ++half)
           for (int dh = 0; dh < 2; ++dh)
@@ -410,7 +412,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           tma_load_3d(slot, &h_map, &m.k_full[s], (j - n) * 64, 0, bh);
         }
       }
-      if (*abort_flag) drain_loads(m.k_full, kStagesK, issued, a.debug_withhold_q ? nullptr : &m.q_full, a.status);
+      if (*abort_flag) drain_loads(m.k_full, kStagesK, issued, WITHHOLD ? nullptr : &m.q_full, a.status);
     }
   } else if (warp == Cfg<NW>::kVWarp) {
     // ------------------------------------------------------------ V producer
@@ -820,15 +822,24 @@ int attn_warpgroups() {
   return nw;
 }
 
+template <bool BF16, int NW, bool WITHHOLD>
+cudaError_t launch_variant(dim3 grid, cudaStream_t stream, const CUtensorMap& q_map, const CUtensorMap& k_map,
+                           const CUtensorMap& v_map, const CUtensorMap& kc_map, const CUtensorMap& vc_map,
+                           const CUtensorMap& h_map, const UmmaArgs& a) {
+  const int smem = static_cast<int>(SmemLayout<NW>::total);
+  const cudaError_t err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<BF16, NW, WITHHOLD>), smem);
+  if (err != cudaSuccess) return err;
+  return launch_pdl(attn_umma_kernel<BF16, NW, WITHHOLD>, grid, dim3(Cfg<NW>::kThreads), size_t(smem), stream,
+                    q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+}
+
 template <bool BF16, int NW>
 cudaError_t launch_nw(dim3 grid, cudaStream_t stream, const CUtensorMap& q_map, const CUtensorMap& k_map,
                       const CUtensorMap& v_map, const CUtensorMap& kc_map, const CUtensorMap& vc_map,
                       const CUtensorMap& h_map, const UmmaArgs& a) {
-  const int smem = static_cast<int>(SmemLayout<NW>::total);
-  const cudaError_t err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<BF16, NW>), smem);
-  if (err != cudaSuccess) return err;
-  return launch_pdl(attn_umma_kernel<BF16, NW>, grid, dim3(Cfg<NW>::kThreads), size_t(smem), stream, q_map, k_map,
-                    v_map, kc_map, vc_map, h_map, a);
+  if (a.debug_withhold_q)
+    return launch_variant<BF16, NW, true>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+  return launch_variant<BF16, NW, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
 }
 
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,

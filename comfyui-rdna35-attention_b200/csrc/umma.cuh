@@ -94,7 +94,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // copy still targets the CTA's shared memory when it exits.  `issued` loads
 // went to stages j % stages; `extra` (may be NULL) is one more barrier whose
 // phase 0 was armed.  Phases the consumers already saw complete at once.
-__device__ __forceinline__ void drain_loads(uint64_t* full, int stages, int issued, uint64_t* extra, int* status) {
+static __device__ __noinline__ void drain_loads(uint64_t* full, int stages, int issued, uint64_t* extra, int* status) {
   int no_abort = 0;
   for (int s = 0; s < stages && s < issued; ++s) {
     const int last = s + ((issued - 1 - s) / stages) * stages;
