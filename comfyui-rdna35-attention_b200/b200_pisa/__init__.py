@@ -402,14 +402,35 @@ def full_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
     return out
 
 
+_MASK_CODES = {torch.bool: 0, torch.float32: 1, torch.float16: 2, torch.bfloat16: 3}
+
+
+def block_mask_bias(mask: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """Pack a [N,T,T] mask view (N = B*H, or 1 for a mask shared by every
+    (batch, head); any strides) into the FP32 [N,T,64] diagonal-block terms
+    the masked fixed-block kernels add to the scores (b2_pack_block_bias).
+    Returns (bias, bias_bh_stride): the stride is T*64, or 0 when N == 1."""
+    if mask.ndim != 3 or mask.shape[1] != mask.shape[2] or mask.dtype not in _MASK_CODES or not mask.is_cuda:
+        raise ValueError("block_mask_bias expects a CUDA [N,T,T] bool or float mask")
+    n, tokens, _ = mask.shape
+    bias = torch.empty((n, tokens, BLOCK_SIZE), device=mask.device, dtype=torch.float32)
+    sb, st, sk = mask.stride()
+    check(LIB.b2_pack_block_bias(mask.data_ptr(), _MASK_CODES[mask.dtype], sb, st, sk, n, tokens, bias.data_ptr(),
+                                 stream_of(mask)))
+    return bias, (tokens * BLOCK_SIZE if n > 1 else 0)
+
+
 def fixed_block_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool = False,
-                          out: torch.Tensor | None = None) -> torch.Tensor:
-    """64-token block-diagonal attention over [B,H,T,D] / [BH,T,D] views."""
+                          out: torch.Tensor | None = None, mask_bias: torch.Tensor | None = None,
+                          mask_bias_stride: int = 0) -> torch.Tensor:
+    """64-token block-diagonal attention over [B,H,T,D] / [BH,T,D] views;
+    ``mask_bias`` (from block_mask_bias) adds each row's mask terms."""
     _checked_device(q.device.index if q.device.index is not None else torch.cuda.current_device())
     if out is None:
         out = torch.empty(q.shape, device=q.device, dtype=q.dtype)
-    check(LIB.b2_fixed_block_attention(ctypes_ref(view(q)), ctypes_ref(view(k)), ctypes_ref(view(v)),
-                                       ctypes_ref(view(out)), _float32(scale), 1 if causal else 0, stream_of(q)))
+    check(LIB.b2_fixed_block_attention_masked(ctypes_ref(view(q)), ctypes_ref(view(k)), ctypes_ref(view(v)),
+                                              ctypes_ref(view(out)), _float32(scale), 1 if causal else 0,
+                                              ptr(mask_bias), int(mask_bias_stride), stream_of(q)))
     return out
 
 
@@ -568,6 +589,7 @@ __all__ = [
     "MAX_BLOCKS",
     "SPATIAL_SPARSE_EXACT_BLOCKS",
     "SPATIAL_TOKENS",
+    "block_mask_bias",
     "block_stats_hyd",
     "build_info",
     "capabilities",

@@ -78,6 +78,9 @@ SIGNATURES: dict[str, tuple] = {
                                                     _I32, _I32, _I32, _F32, _I32, _I32, _VP, _VP]),
     "b2_full_attention": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _F32, _VP, _VP]),
     "b2_fixed_block_attention": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _F32, _I32, _VP]),
+    "b2_fixed_block_attention_masked": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _F32, _I32, _VP, _I64,
+                                                       _VP]),
+    "b2_pack_block_bias": (ctypes.c_int, [_VP, _I32, _I64, _I64, _I64, _I32, _I32, _VP, _VP]),
     "b2_pack_rows": (ctypes.c_int, [_VIEW_P, _VP, _VP]),
     "b2_unpack_rows": (ctypes.c_int, [_VP, _VIEW_P, _VP]),
     "b2_merge_epilogue": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VIEW_P, _VP]),

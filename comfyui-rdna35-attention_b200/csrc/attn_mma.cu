@@ -224,7 +224,10 @@ attn_kernel(const AttnParams p) {
         } else if (p.causal) {
           masked = masked || (kstart + col > q0 + row);
         }
-        s[n][e] = masked ? -INFINITY : val * LOG2E;
+        float x = masked ? -INFINITY : val;
+        if (p.bias != nullptr && !tail && q0 + row < p.tq && col < klen)  // fixed-block mask terms
+          x += p.bias[int64_t(bh) * p.bias_bh_stride + int64_t(q0 + row) * kN + col];
+        s[n][e] = x * LOG2E;
       }
     }
     // ---- online softmax
@@ -334,7 +337,8 @@ attn_kernel(const AttnParams p) {
   // ---- normalise, stage through shared memory, coalesced row stores
   float inv[2];
 #pragma unroll
-  for (int hr = 0; hr < 2; ++hr) inv[hr] = lrow[hr] > 0.f ? 1.f / lrow[hr] : 0.f;
+  for (int hr = 0; hr < 2; ++hr)  // every key masked: NaN, as the reference's softmax gives
+    inv[hr] = lrow[hr] > 0.f ? 1.f / lrow[hr] : (p.bias != nullptr ? __int_as_float(0x7fc00000) : 0.f);
   __syncthreads();  // every warp is done reading qs fragments / H
 #pragma unroll
   for (int n = 0; n < NT; ++n) {

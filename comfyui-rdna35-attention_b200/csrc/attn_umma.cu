@@ -231,8 +231,10 @@ __device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, con
 }
 
 // WITHHOLD (the timeout diagnostics of b2_debug_withhold_q only): the Q tile
-// is never loaded, so the pipeline's bounded waits run out.
-template <bool BF16, int NW, bool WITHHOLD>
+// is never loaded, so the pipeline's bounded waits run out.  MASKED (mode
+// DIAG with a mask): every row adds its FP32 mask terms a.bias to the scaled
+// scores, and a row whose keys are all masked stores NaN.
+template <bool BF16, int NW, bool WITHHOLD, bool MASKED>
 __global__ void __launch_bounds__(Cfg<NW>::kThreads, Cfg<NW>::kCtasPerSm)
 attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                  const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap kc_map,
@@ -535,7 +537,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
       tc_fence_after();
       const uint32_t s_addr = o_base + 128 + 64 * sb;
       const int klen = t.tail ? 64 : min(64, tk_ - t.blk * 64);
-      const bool plain = !t.tail && klen == 64 && !causal_;
+      const bool plain = !MASKED && !t.tail && klen == 64 && !causal_;
       // masked columns of this tile as two 32-bit words (bit c = column c),
       // and the column that carries the last (ragged) block's log2 length
       uint32_t bad0 = 0u, bad1 = 0u;
@@ -590,13 +592,32 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           mx = fmaxf(m0, m1) * scale_log2_;
         } else {
           mx = -INFINITY;
+          if constexpr (MASKED) {
+            // x = (s * scale + mask term) * log2(e); rows past the last token read no terms
+            const float* brow = a.bias + int64_t(bh) * a.bias_bh_stride + int64_t(tq_row) * 64;
+            const bool in_range = tq_row < a.tq;
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const uint32_t bw = c < 32 ? bad0 : bad1;
-            const float x = fmaf(__uint_as_float(v[c]), scale_log2_, c == lastc ? last_bias : bias);
-            const float xm = ((bw >> (c & 31)) & 1u) ? -INFINITY : x;
-            v[c] = __float_as_uint(xm);
-            mx = fmaxf(mx, xm);
+            for (int c = 0; c < 64; c += 4) {
+              const float4 b4 = in_range ? *reinterpret_cast<const float4*>(brow + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t bw = c < 32 ? bad0 : bad1;
+                const float x = fmaf(__uint_as_float(v[c + e]), scale_log2_, bb[e] * 1.4426950408889634f);
+                const float xm = ((bw >> ((c + e) & 31)) & 1u) ? -INFINITY : x;
+                v[c + e] = __float_as_uint(xm);
+                mx = fmaxf(mx, xm);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+              const uint32_t bw = c < 32 ? bad0 : bad1;
+              const float x = fmaf(__uint_as_float(v[c]), scale_log2_, c == lastc ? last_bias : bias);
+              const float xm = ((bw >> (c & 31)) & 1u) ? -INFINITY : x;
+              v[c] = __float_as_uint(xm);
+              mx = fmaxf(mx, xm);
+            }
           }
           mul = 1.f;
         }
@@ -682,7 +703,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
     if (ok && a.has_corr) ok = mbar_wait(&m.c_full, 0, abort_flag, a.status, 11);
     tc_fence_after();
     const bool store = ok && !*abort_flag && (half == 0 || has_b) && tq_row < a.tq;
-    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    const float inv = lt > 0.f ? 1.f / lt : (MASKED ? __int_as_float(0x7fc00000) : 0.f);
     const float cw = tt * a.corr_scale;
     char* orow = store ? a.o.row(bh, tq_row) : nullptr;
     const uint32_t row_base = tmem + lane_base;
@@ -822,14 +843,15 @@ int attn_warpgroups() {
   return nw;
 }
 
-template <bool BF16, int NW, bool WITHHOLD>
+template <bool BF16, int NW, bool WITHHOLD, bool MASKED>
 cudaError_t launch_variant(dim3 grid, cudaStream_t stream, const CUtensorMap& q_map, const CUtensorMap& k_map,
                            const CUtensorMap& v_map, const CUtensorMap& kc_map, const CUtensorMap& vc_map,
                            const CUtensorMap& h_map, const UmmaArgs& a) {
   const int smem = static_cast<int>(SmemLayout<NW>::total);
-  const cudaError_t err = ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<BF16, NW, WITHHOLD>), smem);
+  const cudaError_t err =
+      ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<BF16, NW, WITHHOLD, MASKED>), smem);
   if (err != cudaSuccess) return err;
-  return launch_pdl(attn_umma_kernel<BF16, NW, WITHHOLD>, grid, dim3(Cfg<NW>::kThreads), size_t(smem), stream,
+  return launch_pdl(attn_umma_kernel<BF16, NW, WITHHOLD, MASKED>, grid, dim3(Cfg<NW>::kThreads), size_t(smem), stream,
                     q_map, k_map, v_map, kc_map, vc_map, h_map, a);
 }
 
@@ -838,8 +860,10 @@ cudaError_t launch_nw(dim3 grid, cudaStream_t stream, const CUtensorMap& q_map, 
                       const CUtensorMap& v_map, const CUtensorMap& kc_map, const CUtensorMap& vc_map,
                       const CUtensorMap& h_map, const UmmaArgs& a) {
   if (a.debug_withhold_q)
-    return launch_variant<BF16, NW, true>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
-  return launch_variant<BF16, NW, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+    return launch_variant<BF16, NW, true, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+  if (a.bias != nullptr)
+    return launch_variant<BF16, NW, false, true>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+  return launch_variant<BF16, NW, false, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
 }
 
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,
@@ -885,6 +909,8 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   a.status = status;
   a.trace = p.trace;
   a.debug_withhold_q = p.debug_withhold_q;
+  a.bias = p.mode == 2 ? p.bias : nullptr;
+  a.bias_bh_stride = p.bias_bh_stride;
   a.pairs = p.mode == 1 ? p.pairs : nullptr;
   if (p.nb > 0) {
     const int last_len = kv.tokens - 64 * (p.nb - 1);

@@ -592,25 +592,48 @@ int b2_full_attention(const b2_view* q, const b2_view* k, const b2_view* v, cons
   return ok();
 }
 
-int b2_fixed_block_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, float scale,
-                             int32_t causal, void* stream) {
+int b2_fixed_block_attention_masked(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out,
+                                    float scale, int32_t causal, const float* bias, int64_t bias_bh_stride,
+                                    void* stream) {
   int rc = check_qkv_o(q, k, v, out, true);
   if (rc) return rc;
+  if (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) % 16 || bias_bh_stride < 0 || bias_bh_stride % 4))
+    return fail(B2_ERR_INVALID, "mask bias must be 16-byte aligned with a non-negative stride divisible by 4");
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t err;
   if (q->dtype == B2_F32) {
     if (q->head_dim > 128) return fail(B2_ERR_UNSUPPORTED, "FP32 fixed-block attention supports D <= 128");
     err = launch_fixed_f32(make_rows(*q), make_rows(*k), make_rows(*v), make_rows(*out), q->batch * q->heads, scale,
-                           causal, st);
+                           causal, bias, bias_bh_stride, st);
   } else {
     if (q->head_dim != 32 && q->head_dim != 64 && q->head_dim != 128)
       return fail(B2_ERR_UNSUPPORTED, "fixed-block attention supports D in {32,64,128}");
     AttnParams p = base_params(q, k, v, out, scale);
     p.mode = 2;
     p.causal = causal ? 1 : 0;
+    p.bias = bias;
+    p.bias_bh_stride = bias_bh_stride;
     err = run_attention(q, k, v, out, p, st);
   }
   if (err != cudaSuccess) return cuda_fail(err, "fixed-block attention launch");
+  return ok();
+}
+
+int b2_fixed_block_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, float scale,
+                             int32_t causal, void* stream) {
+  return b2_fixed_block_attention_masked(q, k, v, out, scale, causal, nullptr, 0, stream);
+}
+
+int b2_pack_block_bias(const void* mask, int32_t mask_dtype, int64_t stride_bh, int64_t stride_t, int64_t stride_key,
+                       int32_t mask_bh, int32_t tokens, float* bias, void* stream) {
+  if (mask == nullptr || bias == nullptr) return fail(B2_ERR_INVALID, "mask and bias must be non-NULL");
+  if (mask_bh <= 0 || tokens <= 0) return fail(B2_ERR_INVALID, "mask sizes must be positive");
+  if (mask_dtype < B2_MASK_BOOL || mask_dtype > B2_MASK_BF16) return fail(B2_ERR_INVALID, "unknown mask dtype");
+  if (stride_bh < 0 || stride_t < 0 || stride_key < 0) return fail(B2_ERR_INVALID, "mask strides must be >= 0");
+  if (reinterpret_cast<uintptr_t>(bias) % 16) return fail(B2_ERR_INVALID, "bias must be 16-byte aligned");
+  const cudaError_t err = launch_block_bias(mask, mask_dtype, stride_bh, stride_t, stride_key, mask_bh, tokens, bias,
+                                            static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "mask bias launch");
   return ok();
 }
 

@@ -17,7 +17,8 @@ constexpr int kFRows = 32;  // query rows per CTA: half of a 64-token block
 // shared-memory reads of K^T, P and V are conflict-free or broadcasts.
 // Dot products and P.V sums run over d and key index in ascending order.
 __global__ void __launch_bounds__(kFThreads)
-fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal) {
+fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal, const float* __restrict__ bias,
+                 int64_t bias_bh_stride) {
   extern __shared__ float fs[];
   const int D = q.dim;
   const int QP = D + 1;
@@ -82,8 +83,15 @@ fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal) {
       const int c = tx + 16 * i;
       const bool bad0 = c >= len || (causal && c > r_base + r0);
       const bool bad1 = c >= len || (causal && c > r_base + r1);
-      ps[r0 * 65 + c] = bad0 ? -INFINITY : s0[i] * scale;
-      ps[r1 * 65 + c] = bad1 ? -INFINITY : s1[i] * scale;
+      float x0 = bad0 ? -INFINITY : s0[i] * scale;
+      float x1 = bad1 ? -INFINITY : s1[i] * scale;
+      if (bias != nullptr) {  // mask terms of the row's own block, added after the causal mask
+        const float* brow = bias + int64_t(bh) * bias_bh_stride + int64_t(start + r_base) * kBlock;
+        if (r0 < nr) x0 += brow[r0 * kBlock + c];
+        if (r1 < nr) x1 += brow[r1 * kBlock + c];
+      }
+      ps[r0 * 65 + c] = x0;
+      ps[r1 * 65 + c] = x1;
     }
   }
   __syncthreads();
@@ -101,7 +109,8 @@ fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal) {
     float sum = a + b;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+    // a row with every key masked: NaN, as softmax over all -inf gives
+    const float inv = sum > 0.f ? 1.f / sum : (bias != nullptr ? __int_as_float(0x7fc00000) : 0.f);
     ps[r * 65 + lane] = a * inv;
     ps[r * 65 + lane + 32] = b * inv;
   }
@@ -136,13 +145,14 @@ fixed_f32_kernel(Rows q, Rows k, Rows v, Rows o, float scale, int causal) {
 }  // namespace
 
 cudaError_t launch_fixed_f32(const Rows& q, const Rows& k, const Rows& v, const Rows& o, int batch_heads,
-                             float scale, int causal, cudaStream_t stream) {
+                             float scale, int causal, const float* bias, int64_t bias_bh_stride,
+                             cudaStream_t stream) {
   if (q.dim > 128 || (q.dim & 3) != 0) return cudaErrorInvalidValue;
   const size_t smem = sizeof(float) * (kFRows * (q.dim + 1) + q.dim * 65 + kBlock * q.dim + kFRows * 65);
   cudaError_t err = ensure_smem(reinterpret_cast<const void*>(fixed_f32_kernel), static_cast<int>(smem));
   if (err != cudaSuccess) return err;
   dim3 grid((q.tokens + kBlock - 1) / kBlock, batch_heads, kBlock / kFRows);
-  fixed_f32_kernel<<<grid, kFThreads, smem, stream>>>(q, k, v, o, scale, causal);
+  fixed_f32_kernel<<<grid, kFThreads, smem, stream>>>(q, k, v, o, scale, causal, bias, bias_bh_stride);
   return cudaGetLastError();
 }
 

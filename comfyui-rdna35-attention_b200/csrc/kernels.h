@@ -22,6 +22,8 @@ struct AttnParams {
   int causal;
   long long* trace;
   int debug_withhold_q;  // diagnostics: never load Q, so the pipeline's bounded waits run out
+  const float* bias;     // fixed-block masks: FP32 [BHm][T][64] additive terms, or NULL
+  int64_t bias_bh_stride;  // elements between (batch, head) rows of bias; 0 = one mask for all
   const int32_t* pairs;  // optional [BH][ceil(nq/2)][2] query-block pairing (-1: single)
 };
 // Arguments of the tcgen05 attention kernel (see attn_umma.cu).
@@ -43,6 +45,8 @@ struct UmmaArgs {
   const int32_t* pairs;
   long long* trace;  // optional clock64 timeline of CTA (0,0): [tile][6] + start
   int debug_withhold_q;  // diagnostics (b2_debug_withhold_q): Q is never loaded
+  const float* bias;     // fixed-block mask terms (mode DIAG), see AttnParams
+  int64_t bias_bh_stride;
 };
 bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const b2_view& o);
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,
@@ -73,7 +77,10 @@ cudaError_t launch_merge(const void* exact, const float* exact_lse, const void* 
 cudaError_t launch_centroid_prep(const float* kc, const void* vstat, int vstat_is_sum, int batch_heads, int blocks,
                                  int tokens, int dim, int dtype, void* kc16, void* vc16, cudaStream_t stream);
 cudaError_t launch_fixed_f32(const Rows& q, const Rows& k, const Rows& v, const Rows& o, int batch_heads,
-                             float scale, int causal, cudaStream_t stream);
+                             float scale, int causal, const float* bias, int64_t bias_bh_stride,
+                             cudaStream_t stream);
+cudaError_t launch_block_bias(const void* mask, int mask_dtype, int64_t s_bh, int64_t s_row, int64_t s_col,
+                              int mask_rows_bh, int tokens, float* bias, cudaStream_t stream);
 // Host-side helpers of the C ABI layer (capi.cu): the shared statistics
 // argument checks and the thread-local error string behind b2_last_error.
 int check_stats_call(const b2_view* q, const b2_view* k, const b2_view* v, int mode, const void* q_centroids,

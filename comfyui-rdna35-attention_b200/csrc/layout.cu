@@ -89,6 +89,47 @@ __global__ void centroid_prep_kernel(const float* __restrict__ kc, const void* _
   }
 }
 
+// Diagonal-block bias of an attention mask (reference.py:114-156 slicing +
+// the bool masked_fill / float add of reference.py:182-186): for every mask
+// row (bh, t) of the [BHm, T, T] mask, the 64 entries of t's own key block,
+// as FP32 additive terms: bool True -> 0, False -> -inf, float values as
+// they are; columns past a ragged last block -> -inf.  One thread per
+// (row, 4 columns).
+template <typename M>
+__device__ __forceinline__ float mask_term(const M* p) {
+  return Cvt<M>::to_f(*p);
+}
+template <>
+__device__ __forceinline__ float mask_term<bool>(const bool* p) {
+  return *reinterpret_cast<const unsigned char*>(p) ? 0.f : -INFINITY;
+}
+template <>
+__device__ __forceinline__ float mask_term<float>(const float* p) {
+  return *p;
+}
+
+template <typename M>
+__global__ void block_bias_kernel(const M* __restrict__ mask, int64_t s_bh, int64_t s_row, int64_t s_col, int tokens,
+                                  int64_t n, float* __restrict__ bias) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int64_t row = i >> 4;  // (bh, t)
+    const int c0 = static_cast<int>(i & 15) * 4;
+    const int bh = static_cast<int>(row / tokens);
+    const int t = static_cast<int>(row - int64_t(bh) * tokens);
+    const int start = (t / kBlock) * kBlock;
+    const int len = min(kBlock, tokens - start);
+    const M* src = mask + int64_t(bh) * s_bh + int64_t(t) * s_row;
+    float vals[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = c0 + e;
+      vals[e] = c < len ? mask_term<M>(src + int64_t(start + c) * s_col) : -INFINITY;
+    }
+    *reinterpret_cast<float4*>(bias + row * kBlock + c0) = make_float4(vals[0], vals[1], vals[2], vals[3]);
+  }
+}
+
 inline int grid_for(int64_t n, int threads) {
   int64_t g = (n + threads - 1) / threads;
   const int64_t cap = 148 * 16;
@@ -125,6 +166,30 @@ cudaError_t launch_merge(const void* exact, const float* exact_lse, const void* 
     merge_kernel<__half><<<grid_for(nvec, 256), 256, 0, stream>>>(static_cast<const __half*>(exact), exact_lse,
                                                                   static_cast<const __half*>(approx), approx_lse,
                                                                   corr, dst, nvec, vpr);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_block_bias(const void* mask, int mask_dtype, int64_t s_bh, int64_t s_row, int64_t s_col,
+                              int mask_rows_bh, int tokens, float* bias, cudaStream_t stream) {
+  const int64_t n = int64_t(mask_rows_bh) * tokens * 16;
+  const int g = grid_for(n, 256);
+  switch (mask_dtype) {
+    case B2_MASK_BOOL:
+      block_bias_kernel<bool><<<g, 256, 0, stream>>>(static_cast<const bool*>(mask), s_bh, s_row, s_col, tokens, n,
+                                                     bias);
+      break;
+    case B2_MASK_F32:
+      block_bias_kernel<float><<<g, 256, 0, stream>>>(static_cast<const float*>(mask), s_bh, s_row, s_col, tokens,
+                                                      n, bias);
+      break;
+    case B2_MASK_F16:
+      block_bias_kernel<__half><<<g, 256, 0, stream>>>(static_cast<const __half*>(mask), s_bh, s_row, s_col, tokens,
+                                                       n, bias);
+      break;
+    default:
+      block_bias_kernel<__nv_bfloat16><<<g, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(mask), s_bh, s_row,
+                                                              s_col, tokens, n, bias);
+  }
   return cudaGetLastError();
 }
 

@@ -3,10 +3,12 @@ the reference's rdna35_block_attention/dispatch.py:82-186: same arguments,
 ``mode`` values, diagnostics dict and reason strings).
 
 Eligible calls run the B200 kernel of libb200attn.so directly on the caller's
-layout (BHTD, [BH,T,D] or BTHD viewed as BHTD, no copies).  Requests the
-kernel does not implement -- arbitrary masks, other block sizes, tensors
-that require grad, CPU tensors -- use the PyTorch reference, as the
-reference dispatcher does; on an eligible CUDA call the native library must
+layout (BHTD, [BH,T,D] or BTHD viewed as BHTD, no copies).  Boolean and
+float masks ([T,T], [N,T,T], [B|1,H|1,T,T]) run natively too: their
+diagonal 64x64 blocks are packed on the device into FP32 score terms.
+Requests the kernels do not implement -- masks of other dtypes, other block
+sizes, tensors that require grad, CPU tensors -- use the PyTorch
+reference; on an eligible CUDA call the native library must
 be present (its absence raises instead of silently falling back)."""
 from __future__ import annotations
 
@@ -15,7 +17,7 @@ from typing import Any
 import torch
 
 from . import device
-from .reference import canonical_layout, fixed_block_attention_ref
+from .reference import LayoutInfo, canonical_layout, canonical_mask, fixed_block_attention_ref
 
 SUPPORTED_HEAD_DIMS = {32, 64, 128}
 SUPPORTED_DTYPES = {torch.float16, torch.bfloat16, torch.float32}
@@ -49,8 +51,11 @@ def _layout_of(q, k, v, layout: str, heads: int | None) -> tuple[str, int]:
     raise ValueError(f"layout='{chosen}' does not match a rank-{q.ndim} tensor.")
 
 
+NATIVE_MASK_DTYPES = {torch.bool, torch.float32, torch.float16, torch.bfloat16}
+
+
 def _reject_reason(q_flat, k_flat, v_flat, head_dim, *, block_size, mask) -> str | None:
-    if mask is not None:
+    if mask is not None and (not isinstance(mask, torch.Tensor) or mask.dtype not in NATIVE_MASK_DTYPES):
         return "arbitrary_mask_uses_reference"
     if any(t.requires_grad for t in (q_flat, k_flat, v_flat)):
         return "requires_grad_uses_reference"
@@ -73,6 +78,17 @@ def _reject_reason(q_flat, k_flat, v_flat, head_dim, *, block_size, mask) -> str
     if index is None:
         return "sm100_device_not_detected"
     return None
+
+
+def _mask_bias(mask: torch.Tensor, q_bhtd: torch.Tensor, layout: str):
+    """The mask's diagonal-block terms for the native kernels: the mask is
+    read with the reference's rank rules (canonical_mask) as a [B*H|1,T,T]
+    view and packed on the device."""
+    batch, heads, tokens, dim = q_bhtd.shape
+    known = layout != "bh_t_d"
+    info = LayoutInfo(layout, batch if known else None, heads if known else None, tokens, dim, lambda out: out)
+    full = canonical_mask(mask.to(device=q_bhtd.device), info, batch * heads)
+    return device.native_module().block_mask_bias(full)
 
 
 def _bhtd_view(x: torch.Tensor, layout: str, heads: int | None) -> torch.Tensor:
@@ -107,9 +123,13 @@ def fixed_block_attention(q, k, v, *, block_size: int = 64, scale: float | None 
     scale_value = float(scale) if scale is not None else 1.0 / math.sqrt(head_dim)
     qv, kv, vv = (_bhtd_view(x, chosen, heads) for x in (q, k, v))
     out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    bias, bias_stride = None, 0
     try:
-        native.fixed_block_attention(qv, kv, vv, scale_value, causal, out=_bhtd_view(out, chosen, heads))
-    except ValueError as exc:  # e.g. strides the 16-byte row kernels cannot address
+        if mask is not None:
+            bias, bias_stride = _mask_bias(mask, qv, chosen)
+        native.fixed_block_attention(qv, kv, vv, scale_value, causal, out=_bhtd_view(out, chosen, heads),
+                                     mask_bias=bias, mask_bias_stride=bias_stride)
+    except ValueError as exc:  # e.g. strides the 16-byte row kernels cannot address, or a mask shape
         return _fallback(q, k, v, reason=f"b200_rejected_{exc}", **kwargs)
     diag = {"backend": "b200", "fallback_reason": None, "optimized": True, "layout": chosen,
             "tokens": qv.shape[2], "head_dim": head_dim}

@@ -249,6 +249,28 @@ int b2_fixed_block_attention(const b2_view* q, const b2_view* k,
                              const b2_view* v, const b2_view* out, float scale,
                              int32_t causal, void* stream);
 
+/* ---- Masked fixed-block attention (reference.py:114-200: the diagonal
+ * 64x64 block of a [T,T] / [N,T,T] / [B,H,T,T] mask, boolean masks keeping
+ * True entries, other masks added to the scores).
+ * b2_pack_block_bias reads a mask as [mask_bh, T, T] through element strides
+ * (stride_bh may be 0 for one mask shared by every (batch, head)) and writes
+ * bias [mask_bh, T, 64] FP32: entry (bh, t, c) is the mask term of query t
+ * and key start(t)+c of t's own block (bool: 0 or -inf; float: the value;
+ * -inf past a ragged last block).  b2_fixed_block_attention_masked is
+ * b2_fixed_block_attention with bias[bh * bias_bh_stride + t * 64 + c] added
+ * to the scaled score (after the causal mask); bias_bh_stride is T*64, or 0
+ * for a shared mask.  A query row with every key masked yields NaN, as the
+ * reference's softmax does. */
+enum b2_mask_dtype { B2_MASK_BOOL = 0, B2_MASK_F32 = 1, B2_MASK_F16 = 2, B2_MASK_BF16 = 3 };
+int b2_pack_block_bias(const void* mask, int32_t mask_dtype, int64_t stride_bh,
+                       int64_t stride_t, int64_t stride_key, int32_t mask_bh,
+                       int32_t tokens, float* bias, void* stream);
+int b2_fixed_block_attention_masked(const b2_view* q, const b2_view* k,
+                                    const b2_view* v, const b2_view* out,
+                                    float scale, int32_t causal,
+                                    const float* bias, int64_t bias_bh_stride,
+                                    void* stream);
+
 /* ---- Layout kernels. */
 /* pisa_kernels.cu:247-272: [B,H,T,D] tiled views -> contiguous [BH,T,D]. */
 int b2_pack_rows(const b2_view* src, void* dst, void* stream);

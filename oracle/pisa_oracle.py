@@ -400,10 +400,14 @@ def full_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
 
 
 def fixed_block_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None,
-                          causal: bool = False, block_size: int = BLOCK_SIZE, round_p: bool = False):
+                          causal: bool = False, block_size: int = BLOCK_SIZE, round_p: bool = False,
+                          mask: torch.Tensor | None = None):
     """reference.py:159-200 on [..., T, D]: each 64-token query block attends to
     its own key block, FP32.  round_p=True rounds P to the input dtype before
-    P.V, as the 16-bit Triton kernel does (triton_kernel.py:96)."""
+    P.V, as the 16-bit Triton kernel does (triton_kernel.py:96).  mask: a
+    tensor broadcastable to [..., T, T] (reference.py:114-156 after its
+    rank rules): boolean masks keep True entries, others are added to the
+    scaled scores after the causal mask; a fully masked row gives NaN."""
     t, d = q.shape[-2], q.shape[-1]
     scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
     out = torch.empty(q.shape, dtype=torch.float32)
@@ -413,6 +417,9 @@ def fixed_block_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sca
         if causal:
             m = torch.ones((e - s, e - s), dtype=torch.bool).triu(1)
             sc = sc.masked_fill(m, -torch.inf)
+        if mask is not None:
+            blk = mask[..., s:e, s:e]
+            sc = sc.masked_fill(~blk, -torch.inf) if blk.dtype == torch.bool else sc + blk.float()
         p = torch.softmax(sc, dim=-1)
         if round_p:
             p = p.to(q.dtype).float()

@@ -4,7 +4,7 @@ import sys
 import pytest
 
 ROOT = pathlib.Path(__file__).resolve().parents[1]
-for p in (ROOT / "comfyui-rdna35-attention_b200", ROOT / "oracle", ROOT / "tests"):
+for p in (ROOT / "comfyui-rdna35-attention_b200", ROOT / "oracle", ROOT / "tests", ROOT / "tests" / "golden"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
 

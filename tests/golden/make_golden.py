@@ -5,7 +5,9 @@ Run in the container that has the reference checkout (read-only):
 It imports the reference's own Python implementations -- never the product
 package -- and writes tests/golden/golden.pt:
   * fixed_block: rdna35_block_attention.reference.fixed_block_attention_ref
-    (config 1 shape scaled to 2 heads x 256 tokens; plain and causal);
+    (config 1 shape scaled to 2 heads x 256 tokens; plain and causal), and
+    fixed_block_masked: the same with [T,T] / [N,T,T] / [B,H,T,T] boolean and
+    additive float masks (ragged T=130, causal, fully masked rows -> NaN);
   * pisa_hyd: _pisa_reference of native/rdna35_pisa_ck/tests/test_forward.py
     (the reference's own pure-torch HYD oracle; the native wheel it imports
     is stubbed because it cannot load without its ROCm build) for T in
@@ -32,6 +34,29 @@ def seeded(shape, seed, dtype=torch.float32):
     return torch.randn(shape, generator=gen).to(dtype)
 
 
+MASK_CASES = [
+    {"name": "bool_2d", "shape": (130, 130), "kind": "bool", "causal": False, "seed": 500},
+    {"name": "bool_3d_per_batch", "shape": (1, 130, 130), "kind": "bool", "causal": True, "seed": 510},
+    {"name": "bool_4d_per_head", "shape": (1, 2, 130, 130), "kind": "bool", "causal": False, "seed": 520},
+    {"name": "float_3d_per_bh", "shape": (2, 130, 130), "kind": "float", "causal": False, "seed": 530},
+    {"name": "bool_2d_dead_rows", "shape": (130, 130), "kind": "bool_dead_rows", "causal": False, "seed": 540},
+]
+
+
+def make_mask(case):
+    """The mask of one masked case, regenerated from its seed (bool: keep
+    ~70% of entries; float: N(0,1) terms; dead rows: rows 3 and 70 masked
+    entirely)."""
+    gen = torch.Generator().manual_seed(case["seed"] + 99)
+    if case["kind"] == "float":
+        return torch.randn(case["shape"], generator=gen)
+    mask = torch.rand(case["shape"], generator=gen) > 0.3
+    if case["kind"] == "bool_dead_rows":
+        mask[3] = False
+        mask[70] = False
+    return mask
+
+
 def block_offset_inputs(tokens, seed, dtype=torch.bfloat16):
     """[1,T,128] N(0,1) plus a per-64-token-block N(0,0.5) offset (config 3's
     value distribution in block-major order)."""
@@ -55,12 +80,20 @@ def main(ref_root: str) -> None:
     spec.loader.exec_module(test_forward)
     pisa_reference = test_forward._pisa_reference
 
-    golden: dict = {"fixed_block": [], "pisa_hyd": [], "pisa_hyd_full": [], "pisa_paper": [], "tiling": {}, "h3_pack": {}}
+    golden: dict = {"fixed_block": [], "fixed_block_masked": [], "pisa_hyd": [], "pisa_hyd_full": [], "pisa_paper": [], "tiling": {}, "h3_pack": {}}
     for causal in (False, True):
         q, k, v = (seeded((1, 2, 256, 64), 100 + i) for i in range(3))
         out = fixed_block_attention_ref(q, k, v, block_size=64, scale=0.125, causal=causal, layout="bhtd")
         golden["fixed_block"].append({"seeds": (100, 101, 102), "shape": (1, 2, 256, 64), "scale": 0.125,
                                       "causal": causal, "out": out})
+    # masked fixed-block cases (reference.py:114-200): mask forms by rank,
+    # bool and additive float, with causal, ragged T and fully masked rows
+    for case in MASK_CASES:
+        q, k, v = (seeded((1, 2, 130, 32), case["seed"] + i) for i in range(3))
+        mask = make_mask(case)
+        out = fixed_block_attention_ref(q, k, v, block_size=64, scale=None, causal=case["causal"], layout="bhtd",
+                                        mask=mask)
+        golden["fixed_block_masked"].append({**case, "out": out})
     for tokens, exact, sink, seed in ((128, 1, None, 19), (65, 1, 0, 23), (65, 1, -1, 23), (256, 2, None, 31),
                                       (256, 0, None, 37), (128, 2, None, 17)):
         q, k, v = (seeded((1, tokens, 128), seed * 10 + i, torch.bfloat16) for i in range(3))

@@ -149,7 +149,12 @@ def test_dispatch_reasons_on_cpu():
     assert out.shape == q.shape and info["backend"] == "reference" and "not_cuda" in info["fallback_reason"]
     _, info = fixed_block_attention(q, q, q, block_size=32, layout="bhtd", return_diagnostics=True)
     assert "unsupported_block_size_32" in info["fallback_reason"]
+    # float and bool masks run natively on a GPU; on the CPU the device decides
     _, info = fixed_block_attention(q, q, q, layout="bhtd", mask=torch.zeros(64, 64), return_diagnostics=True)
+    assert "not_cuda" in info["fallback_reason"]
+    # masks of other dtypes keep the reference's reason
+    _, info = fixed_block_attention(q, q, q, layout="bhtd", mask=torch.zeros(64, 64, dtype=torch.int32),
+                                    return_diagnostics=True)
     assert "arbitrary_mask" in info["fallback_reason"]
     qg = torch.randn(1, 1, 64, 32, dtype=torch.float16, requires_grad=True)
     _, info = fixed_block_attention(qg, qg, qg, layout="bhtd", return_diagnostics=True)

@@ -103,3 +103,21 @@ def test_hyd_oracle_matches_reference_at_full_anima_size(case):
     loop, idx_l = oracle.hyd_forward(q, k, v, case["exact_blocks"], sink_block=case["sink_block"], stats=stats)
     assert torch.equal(idx_b, idx_l)
     torch.testing.assert_close(batched.float(), loop.float(), atol=1e-2, rtol=1e-2)  # matmul blocking order
+
+
+@pytest.mark.parametrize("case", GOLDEN["fixed_block_masked"], ids=lambda c: c["name"])
+def test_masked_fixed_block_oracle_matches_reference(case):
+    """Masked fixed-block attention: the oracle, given the mask broadcast to
+    [B,H,T,T] by the reference's rank rules, reproduces the reference's
+    outputs, NaN rows included."""
+    import make_golden
+
+    q, k, v = (seeded((1, 2, 130, 32), case["seed"] + i) for i in range(3))
+    mask = make_golden.make_mask(case)
+    if mask.ndim == 3 and mask.shape[0] == 1:  # [B,T,T] with B=1: one mask per batch
+        mask = mask[:, None]
+    elif mask.ndim == 3:  # [BH,T,T]
+        mask = mask.view(1, 2, 130, 130)
+    out = oracle.fixed_block_attention(q, k, v, causal=case["causal"], mask=mask)
+    assert torch.equal(torch.isnan(out), torch.isnan(case["out"]))
+    torch.testing.assert_close(out.nan_to_num(), case["out"].nan_to_num(), atol=1e-5, rtol=1e-5)
