@@ -361,16 +361,18 @@ def generic_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blo
                     out: torch.Tensor | None = None, return_indices: bool = False):
     """Generic PISA (generic_pisa.py:141-232 semantics): FP32 centroids,
     routing without the HYD bias, 16-bit-rounded centred K, optional
-    first-order term.  q/k/v: [BH,T,128] or [B,H,T,128] views (fp16/bf16,
-    head dimension contiguous), T up to 65536.  grid=(h, w) reads the tokens
+    first-order term.  q/k/v: [BH,T,D] or [B,H,T,D] views (fp16/bf16,
+    head dimension contiguous, D <= 128 a multiple of 8: the kernels' TMA
+    tiles read the columns past D as zeros, so no padded copy is made), T up
+    to 65536.  grid=(h, w) reads the tokens
     in 8x8-tile order of per-frame h x w rasters (no packing copy); the
     output (``out`` view or a new tensor shaped like q) is in token order.
     return_indices=True also returns the routed key blocks, int32
     [BH,nb,exact_blocks] ascending (diagnostics; sparse calls only)."""
     if q.ndim not in (3, 4) or q.shape != k.shape or q.shape != v.shape:
         raise ValueError("generic PISA requires matching [BH,T,D] or [B,H,T,D] q/k/v")
-    if q.shape[-1] != HEAD_DIM:
-        raise ValueError(f"B200 generic PISA requires D={HEAD_DIM}")
+    if q.shape[-1] > HEAD_DIM or q.shape[-1] % 8:
+        raise ValueError(f"B200 generic PISA requires D <= {HEAD_DIM}, a multiple of 8")
     tokens = q.shape[-2]
     blocks = (tokens + BLOCK_SIZE - 1) // BLOCK_SIZE
     if blocks > GENERIC_MAX_BLOCKS:

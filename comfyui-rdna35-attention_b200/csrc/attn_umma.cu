@@ -732,9 +732,16 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           packed[c / 2] = Cvt<T>::pack2(f0 * inv, f1 * inv);
         }
         uint4* dst = reinterpret_cast<uint4*>(orow + c0 * 2);
+        if (a.o.dim == 128) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          dst[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+          for (int q4 = 0; q4 < 4; ++q4)
+            dst[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+        } else {  // head dim < 128: the columns past D were zero-filled inputs, not outputs
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            if (c0 + 8 * q4 < a.o.dim)
+              dst[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+        }
       }
     }
     if (store && wg == 0 && a.lse != nullptr) {
@@ -822,14 +829,16 @@ int* device_status_ptr() {
 }
 
 bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const b2_view& o) {
-  if (q.head_dim != 128 || q.dtype == B2_F32) return false;
+  // D < 128 (multiples of 8): the TMA boxes stay 64 columns wide and read
+  // the columns past D as zeros, which changes no dot product
+  if (q.head_dim > 128 || q.head_dim % 8 || q.dtype == B2_F32) return false;
+  if (o.head_dim != q.head_dim || v.head_dim != q.head_dim) return false;
   for (const b2_view* x : {&q, &k, &v}) {
     if (x->order == B2_ORDER_TILED8) {
       const int64_t frame = int64_t(x->grid_h) * x->grid_w;
       if (x->batch > 1 && x->stride_b != (x->tokens / frame) * frame * x->stride_t) return false;
     }
   }
-  (void)o;
   return encode_fn() != nullptr;
 }
 

@@ -74,13 +74,19 @@ cudaError_t run_stats(const b2_view* q, const b2_view* k, const b2_view* v, int 
       if (launched) return launch_stats_reduce(partial, (nb + group - 1) / group, bh, h_sum, h_half, q->dtype, st);
     }
   }
+  // the warp-MMA statistics kernel reads 128 columns: D < 128 needs the TMA path
+  if (q->head_dim != 128) return cudaErrorNotSupported;
   return launch_stats(make_rows(*q), make_rows(*k), make_rows(*v), q->dtype, mode, bh, nb, qc, kc, vs, h_sum, h_norm,
                       h_half, partial, st);
 }
 
 cudaError_t run_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* o, const AttnParams& p,
                           cudaStream_t st) {
-  if (umma_enabled() && umma_supported(*q, *k, *v, *o)) {
+  // D = 32 / 64 full and fixed-block attention keep the warp-MMA kernel,
+  // which computes at D; other D < 128 run zero-filled on the tcgen05 kernel
+  const bool mma_native = q->head_dim == 32 || q->head_dim == 64 || q->head_dim == 128;
+  const bool prefer_umma = q->head_dim == 128 || p.mode == 1 || !mma_native;
+  if (umma_enabled() && prefer_umma && umma_supported(*q, *k, *v, *o)) {
     AttnParams pt = p;
     pt.trace = g_trace;
     pt.debug_withhold_q = g_withhold_q;
@@ -94,6 +100,7 @@ cudaError_t run_attention(const b2_view* q, const b2_view* k, const b2_view* v, 
       }
     }
   }
+  if (!mma_native || (p.mode == 1 && q->head_dim != 128)) return cudaErrorNotSupported;
   g_last_kernel = "mma_sync";
   return launch_attn_mma(p, q->dtype, q->batch * q->heads, st);
 }
@@ -441,7 +448,8 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
   int rc = check_qkv_o(q, k, v, out, true);
   if (rc) return rc;
   if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA supports bfloat16 and float16");
-  if (q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "PISA requires D=128");
+  if (q->head_dim > 128 || q->head_dim % 8 || (stats_mode == B2_STATS_HYD && q->head_dim != 128))
+    return fail(B2_ERR_UNSUPPORTED, "PISA requires D=128 (generic PISA: D <= 128, a multiple of 8)");
   if (!(scale > 0.f) || !(scale < 3.4028235e38f))
     return fail(B2_ERR_INVALID, "scale must be representable as a positive finite float32 value.");
   const int nb = (q->tokens + kBlock - 1) / kBlock;
@@ -464,16 +472,17 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
     return ok();
   }
   if (workspace == nullptr) return fail(B2_ERR_INVALID, "workspace must be non-NULL");
-  PisaWorkspace w = carve(static_cast<char*>(workspace), bh, q->tokens, q->head_dim, exact_blocks);
+  // centroids, H and the tail tiles are 128 wide; columns past D stay zero
+  PisaWorkspace w = carve(static_cast<char*>(workspace), bh, q->tokens, kTileDim, exact_blocks);
   const bool hyd = stats_mode == B2_STATS_HYD;
   err = run_stats(q, k, v, stats_mode, w.qc, w.kc, w.vstat, w.hsum, hyd ? w.hnorm : nullptr, w.h16, w.partial, st);
   if (err != cudaSuccess) return cuda_fail(err, "PISA statistics launch");
-  err = launch_centroid_prep(w.kc, w.vstat, hyd ? 0 : 1, bh, nb, q->tokens, q->head_dim, q->dtype, w.kc16, w.vc16, st);
+  err = launch_centroid_prep(w.kc, w.vstat, hyd ? 0 : 1, bh, nb, q->tokens, kTileDim, q->dtype, w.kc16, w.vc16, st);
   if (err != cudaSuccess) return cuda_fail(err, "PISA centroid preparation launch");
   const int words = (nb + 31) / 32;
   if (exact_blocks > 0) {
     err = launch_route(w.qc, hyd ? B2_BF16 : B2_F32, w.kc, hyd ? B2_BF16 : B2_F32, hyd ? w.hnorm : nullptr, bh, nb,
-                       q->head_dim, exact_blocks, scale, hyd ? sink_block : -2, w.indices, w.sel, st);
+                       kTileDim, exact_blocks, scale, hyd ? sink_block : -2, w.indices, w.sel, st);
     if (err != cudaSuccess) return cuda_fail(err, "PISA routing launch");
   } else {
     err = cudaMemsetAsync(w.sel, 0, size_t(bh) * nb * words * 4, st);
@@ -583,7 +592,8 @@ int b2_full_attention(const b2_view* q, const b2_view* k, const b2_view* v, cons
   int rc = check_qkv_o(q, k, v, out, false);
   if (rc) return rc;
   if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "full attention supports float16 and bfloat16");
-  if (q->head_dim != 64 && q->head_dim != 128) return fail(B2_ERR_UNSUPPORTED, "full attention supports D in {64,128}");
+  if (q->head_dim > 128 || q->head_dim % 8)
+    return fail(B2_ERR_UNSUPPORTED, "full attention supports D <= 128, a multiple of 8");
   AttnParams p = base_params(q, k, v, out, scale);
   p.mode = 0;
   p.lse = lse;

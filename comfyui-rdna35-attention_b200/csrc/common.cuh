@@ -12,6 +12,7 @@
 namespace b2 {
 
 constexpr int kBlock = 64;  // PISA / fixed-block token block
+constexpr int kTileDim = 128;  // head-dim width of the tcgen05 tiles and the PISA workspace rows
 
 // Device-side copy of a b2_view (pointer + strides + token order).
 struct Rows {

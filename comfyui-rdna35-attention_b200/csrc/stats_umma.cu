@@ -437,7 +437,10 @@ cudaError_t launch_stats_umma(const b2_view& q, const b2_view& k, const b2_view&
                               void* q_centroids, float* k_centroids, void* v_stats, float* h_norm, float* partial,
                               int* status, cudaStream_t stream, bool* launched) {
   *launched = false;
-  if (q.head_dim != 128 || q.dtype == B2_F32 || (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC)) return cudaSuccess;
+  // D < 128 (multiples of 8): columns past D load as zeros (TMA fill), so
+  // centroids and H carry zeros there
+  if (q.head_dim > 128 || q.head_dim % 8 || q.dtype == B2_F32 || (mode != B2_STATS_HYD && mode != B2_STATS_GENERIC))
+    return cudaSuccess;
   CUtensorMap qm, km, vm;
   int qk = 0, kk = 0, vk = 0;
   if (!stats_map(&qm, q, &qk) || !stats_map(&km, k, &kk) || !stats_map(&vm, v, &vk) || qk != kk || kk != vk)

@@ -19,7 +19,7 @@ from . import device
 
 BLOCK_SIZE = 64
 MIN_TOKENS = 8192
-NATIVE_HEAD_DIM = 128  # the kernels' head dimension; smaller heads are zero-padded
+NATIVE_HEAD_DIM = 128  # the kernels' tile width; smaller heads are zero-filled by the TMA loads
 SPATIAL_BLOCK_EDGE = 8
 
 
@@ -90,24 +90,9 @@ def generic_pisa_attention(q, k, v, *, exact_budget: float, scale: float | None 
     exact_blocks = min(blocks, max(1, math.ceil(exact_budget * blocks)))
     scale_value = float(scale) if scale is not None else 1.0 / math.sqrt(head_dim)
     native = device.native_module()
-    if head_dim < NATIVE_HEAD_DIM:
-        # SD1.5-style heads (D = 40, 64, 80 ...): zero columns up to D = 128
-        # change no dot product, centroid, routing score or first-order term,
-        # so the padded call computes the same attention; the extra output
-        # columns are dropped
-        pad = NATIVE_HEAD_DIM - head_dim
-        qp, kp, vp = (F.pad(t, (0, pad)) for t in (q, k, v))
-        if exact_blocks == blocks:
-            padded = native.full_attention(qp, kp, vp, scale_value)
-        else:
-            padded = native.generic_forward(qp, kp, vp, exact_blocks, scale_value, first_order=use_first_order,
-                                            grid=token_grid)
-        output = padded[..., :head_dim]
-        if out is not None:
-            out.copy_(output)
-            output = out
-        backend = "dense_b200" if exact_blocks == blocks else ("b200_hyd" if use_first_order else "b200_0th")
-        return (output, backend) if return_backend else output
+    # SD1.5 / SDXL heads (D = 40, 64, 80 ...) run at their own D: the
+    # kernels' 128-wide TMA tiles load the columns past D as zeros, which
+    # changes no dot product, centroid, routing score or first-order term
     if exact_blocks == blocks:
         output = native.full_attention(q, k, v, scale_value, out=out)
         return (output, "dense_b200") if return_backend else output

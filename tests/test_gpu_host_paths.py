@@ -116,7 +116,7 @@ def test_anima_attn_op_end_to_end():
 @pytest.mark.parametrize("head_dim,dtype,first_order", [(40, torch.bfloat16, False), (80, torch.bfloat16, False),
                                                         (64, torch.float16, False), (40, torch.bfloat16, True)])
 def test_generic_pisa_small_head_dims_match_oracle(head_dim, dtype, first_order):
-    # SD1.5-style heads run zero-padded to D=128 (same attention, extra columns dropped)
+    # SD1.5-style heads run at their own D (TMA tiles zero-fill the columns past D)
     from rdna35_block_attention.generic_pisa import generic_pisa_attention
 
     tokens, bh = 8320, 2
@@ -162,3 +162,24 @@ def test_generic_override_runs_d80_natively_and_d160_falls_back():
     original = mock.Mock(return_value="previous")
     assert override(original, q160, q160, q160, heads, is_self_attention=True) == "previous"
     assert any("pisa_backend_error" in r for r in state.fallback_reasons), state.report()
+
+
+@pytest.mark.parametrize("head_dim", [40, 80, 96])
+def test_generic_pisa_small_head_dims_tiled_and_dense(head_dim):
+    """D < 128 through the tiled (8x8 per-frame) token order, and dense full
+    attention at D = 40 / 80 / 96 on the tcgen05 kernel, against the oracle."""
+    import b200_pisa
+
+    gen = torch.Generator().manual_seed(head_dim + 1)
+    grid, tokens = (96, 96), 9216
+    q, k, v = (torch.randn((1, 2, tokens, head_dim), generator=gen).to(torch.bfloat16) for _ in range(3))
+    out = b200_pisa.generic_forward(q.to(DEV), k.to(DEV), v.to(DEV), 23, head_dim ** -0.5, grid=grid).cpu()
+    perm = oracle.raster_permutation(tokens, *grid)
+    packed = [x[:, :, perm].reshape(2, tokens, head_dim) for x in (q, k, v)]
+    exp, _ = oracle.generic_forward(*packed, 23, scale=head_dim ** -0.5)
+    unperm = torch.empty_like(exp)
+    unperm[:, perm] = exp
+    torch.testing.assert_close(out.reshape(2, tokens, head_dim).float(), unperm.float(), atol=5e-2, rtol=5e-2)
+    dense = b200_pisa.full_attention(q.to(DEV), k.to(DEV), v.to(DEV), head_dim ** -0.5)
+    ref, _ = oracle.full_attention(q, k, v, head_dim ** -0.5)
+    torch.testing.assert_close(dense.cpu().float(), ref.float(), atol=2e-2, rtol=2e-2)
