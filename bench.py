@@ -65,8 +65,8 @@ CORR_FLOP = 2.0 * B * H * T * D * D                       # 9.66 GFLOP
 STATS_BYTES = 3 * B * H * T * D * 2                       # q/k/v read once
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu
 # capture of this workload's attention and statistics kernels
-ATTN_TRAFFIC = 290.8e6
-STATS_TRAFFIC = 241.7e6
+ATTN_TRAFFIC = 288.8e6
+STATS_TRAFFIC = 240.2e6
 CONFIG = {
     "workload": "anima_pisa_hyd_spatial",
     "batch": B, "heads": H, "tokens": T, "head_dim": D, "exact_blocks": EXACT, "blocks": NB,
