@@ -4,13 +4,22 @@ Every (batch, head) of a PISA call is independent: the statistics, routing
 and attention of one head never read another head's data (the reference's
 kernels grid over batch*heads, native/rdna35_pisa_ck/csrc/pisa_kernels.cu:583,
 and its FlexAttention call is per (batch, head)).  A call over H heads on N
-GPUs (one process per GPU, torch.distributed with NCCL) therefore splits the
-heads into N contiguous ranges: each rank computes its range with the
-single-GPU kernels, then one NCCL all-gather exchanges the outputs over
-NVLink, and a 16-byte copy kernel interleaves the gathered [N,B,T,Hs*D]
-shards into the caller's [B,T,H*D] raster.  Because a head's output does
-not depend on which other heads share its call, the sharded result equals
-the single-GPU result bit for bit.
+GPUs (one process per GPU, torch.distributed) therefore splits the heads
+into N contiguous ranges, each rank computing its range with the single-GPU
+kernels.  The outputs are exchanged in one of two ways:
+
+* ``exchange="peer"`` (default): the output lives in a symmetric buffer
+  (``torch.distributed._symmetric_memory``: every rank's copy mapped into
+  every process) and the attention kernel's epilogue stores each output row
+  both locally and into every peer's copy over NVLink
+  (``b2_pisa_forward_mirrored``), so the exchange overlaps the attention
+  itself; two device-side barriers bracket the call.
+* ``exchange="nccl"``: each rank computes into a local [B,T,Hs*D] buffer, one
+  NCCL all-gather exchanges the shards and a 16-byte copy kernel interleaves
+  the gathered [N,B,T,Hs*D] shards into the [B,T,H*D] raster.
+
+Because a head's output does not depend on which other heads share its call,
+the sharded result equals the single-GPU result bit for bit.
 """
 from __future__ import annotations
 
@@ -20,6 +29,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
+
+_SYMMETRIC: dict = {}
 
 
 def head_range(heads: int, world: int, rank: int) -> tuple[int, int]:
@@ -69,16 +80,66 @@ def gather_head_shards(local: torch.Tensor, group=None, out: torch.Tensor | None
     return interleave_shards(gathered.view(world, *local.shape), out)
 
 
+def _symmetric_output(shape: tuple, dtype: torch.dtype, device: torch.device, group):
+    """(buffer, handle) of a symmetric [B,T,H*D] output buffer for `group`,
+    allocated and exchanged once per (shape, dtype, device, group)."""
+    import torch.distributed._symmetric_memory as symm_mem
+
+    group = group if group is not None else dist.group.WORLD
+    key = (tuple(shape), dtype, device, group.group_name)
+    if key not in _SYMMETRIC:
+        buf = symm_mem.empty(shape, dtype=dtype, device=device)
+        handle = symm_mem.rendezvous(buf, group)
+        _SYMMETRIC[key] = (buf, handle)
+    return _SYMMETRIC[key]
+
+
 def forward_spatial_bhtd_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int,
                                  scale: float | None = None, sink_block: int | None = None, *, group=None,
-                                 out: torch.Tensor | None = None) -> torch.Tensor:
+                                 out: torch.Tensor | None = None, exchange: str = "peer") -> torch.Tensor:
     """Anima spatial PISA over the heads of all ranks of `group`.
 
     q/k/v: this rank's head shard, BHTD views [B,Hs,9216,128] of contiguous
     [B,9216,Hs,128] BF16 storage (heads head_range(H, N, rank) of the full
     call).  Returns the full [B,9216,N*Hs*128] raster output on every rank,
-    equal to forward_spatial_bhtd over all H heads on one GPU."""
-    from . import forward_spatial_bhtd
+    equal to forward_spatial_bhtd over all H heads on one GPU.  With
+    exchange="peer" the returned tensor is the group's symmetric output
+    buffer, valid until the next peer-exchange call of the same shape on the
+    group (pass ``out`` to receive a copy instead)."""
+    from . import (HEAD_DIM, SPATIAL_SIDE, _check_exact_and_sink, _checked_device, _float32,
+                   _validate_spatial_bhtd, _workspace, forward_spatial_bhtd)
 
-    local = forward_spatial_bhtd(q, k, v, exact_blocks, scale=scale, sink_block=sink_block)
-    return gather_head_shards(local, group=group, out=out)
+    if exchange not in ("peer", "nccl"):
+        raise ValueError("exchange must be 'peer' or 'nccl'")
+    world = dist.get_world_size(group)
+    if exchange == "nccl" or world == 1:
+        local = forward_spatial_bhtd(q, k, v, exact_blocks, scale=scale, sink_block=sink_block)
+        return gather_head_shards(local, group=group, out=out)
+    _validate_spatial_bhtd(q, k, v)
+    batch, heads, tokens, dim = q.shape
+    blocks = tokens // 64
+    _check_exact_and_sink(exact_blocks, blocks, sink_block)
+    rank = dist.get_rank(group)
+    _checked_device(q.device.index)
+    if world - 1 > 7:
+        raise ValueError("the peer exchange supports at most 8 ranks")
+    full, handle = _symmetric_output((batch, tokens, world * heads * dim), q.dtype, q.device, group)
+    h0 = rank * heads
+    local = full.view(batch, tokens, world * heads, dim)[:, :, h0:h0 + heads]
+    tiled = dict(order=_lib.ORDER_TILED8, grid=(SPATIAL_SIDE, SPATIAL_SIDE))
+    qv, kv, vv = (_lib.view(x, **tiled) for x in (q, k, v))
+    ov = _lib.view(local.permute(0, 2, 1, 3), **tiled)
+    peers = [handle.buffer_ptrs[p] for p in range(world) if p != rank]
+    mirrors = (ctypes.c_void_p * len(peers))(*peers)
+    ws = _workspace(q.device, batch * heads, tokens, exact_blocks) if exact_blocks < blocks else None
+    scale_value = _float32(1.0 / (HEAD_DIM ** 0.5) if scale is None else scale)
+    handle.barrier(channel=0)  # every rank is done with the buffer's previous contents
+    _lib.check(_lib.LIB.b2_pisa_forward_mirrored(
+        ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(ov), exact_blocks, scale_value,
+        -2 if sink_block is None else sink_block, _lib.STATS_HYD, 1, full.data_ptr(),
+        full.numel() * full.element_size(), mirrors, len(peers), _lib.ptr(ws), _lib.stream_of(q)))
+    handle.barrier(channel=1)  # every rank's rows have landed in every copy
+    if out is not None:
+        out.copy_(full)
+        return out
+    return full

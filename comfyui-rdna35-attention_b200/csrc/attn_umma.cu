@@ -233,8 +233,10 @@ __device__ __forceinline__ bool issue_pv(Misc& m, char* smem, uint32_t tmem, con
 // WITHHOLD (the timeout diagnostics of b2_debug_withhold_q only): the Q tile
 // is never loaded, so the pipeline's bounded waits run out.  MASKED (mode
 // DIAG with a mask): every row adds its FP32 mask terms a.bias to the scaled
-// scores, and a row whose keys are all masked stores NaN.
-template <bool BF16, int NW, bool WITHHOLD, bool MASKED>
+// scores, and a row whose keys are all masked stores NaN.  MIRROR (head-
+// sharded calls): every output row is also stored into a.n_mirror peer
+// copies of the output buffer.
+template <bool BF16, int NW, bool WITHHOLD, bool MASKED, bool MIRROR>
 __global__ void __launch_bounds__(Cfg<NW>::kThreads, Cfg<NW>::kCtasPerSm)
 attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                  const __grid_constant__ CUtensorMap v_map, const __grid_constant__ CUtensorMap kc_map,
@@ -742,6 +744,18 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
             if (c0 + 8 * q4 < a.o.dim)
               dst[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
         }
+        if constexpr (MIRROR) {
+          // the same 16-byte stores into the other GPUs' copies of the output
+          // buffer (peer memory over NVLink), at the same offset
+          const int64_t off = (orow - a.o.base) + c0 * 2;
+          for (int mi = 0; mi < a.n_mirror; ++mi) {
+            uint4* md = reinterpret_cast<uint4*>(a.mirror[mi] + off);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              if (c0 + 8 * q4 < a.o.dim)
+                md[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+          }
+        }
       }
     }
     if (store && wg == 0 && a.lse != nullptr) {
@@ -852,15 +866,15 @@ int attn_warpgroups() {
   return nw;
 }
 
-template <bool BF16, int NW, bool WITHHOLD, bool MASKED>
+template <bool BF16, int NW, bool WITHHOLD, bool MASKED, bool MIRROR>
 cudaError_t launch_variant(dim3 grid, cudaStream_t stream, const CUtensorMap& q_map, const CUtensorMap& k_map,
                            const CUtensorMap& v_map, const CUtensorMap& kc_map, const CUtensorMap& vc_map,
                            const CUtensorMap& h_map, const UmmaArgs& a) {
   const int smem = static_cast<int>(SmemLayout<NW>::total);
   const cudaError_t err =
-      ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<BF16, NW, WITHHOLD, MASKED>), smem);
+      ensure_smem(reinterpret_cast<const void*>(attn_umma_kernel<BF16, NW, WITHHOLD, MASKED, MIRROR>), smem);
   if (err != cudaSuccess) return err;
-  return launch_pdl(attn_umma_kernel<BF16, NW, WITHHOLD, MASKED>, grid, dim3(Cfg<NW>::kThreads), size_t(smem), stream,
+  return launch_pdl(attn_umma_kernel<BF16, NW, WITHHOLD, MASKED, MIRROR>, grid, dim3(Cfg<NW>::kThreads), size_t(smem), stream,
                     q_map, k_map, v_map, kc_map, vc_map, h_map, a);
 }
 
@@ -869,10 +883,12 @@ cudaError_t launch_nw(dim3 grid, cudaStream_t stream, const CUtensorMap& q_map, 
                       const CUtensorMap& v_map, const CUtensorMap& kc_map, const CUtensorMap& vc_map,
                       const CUtensorMap& h_map, const UmmaArgs& a) {
   if (a.debug_withhold_q)
-    return launch_variant<BF16, NW, true, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+    return launch_variant<BF16, NW, true, false, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
   if (a.bias != nullptr)
-    return launch_variant<BF16, NW, false, true>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
-  return launch_variant<BF16, NW, false, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+    return launch_variant<BF16, NW, false, true, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+  if (a.n_mirror > 0)
+    return launch_variant<BF16, NW, false, false, true>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
+  return launch_variant<BF16, NW, false, false, false>(grid, stream, q_map, k_map, v_map, kc_map, vc_map, h_map, a);
 }
 
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,
@@ -920,6 +936,8 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   a.debug_withhold_q = p.debug_withhold_q;
   a.bias = p.mode == 2 ? p.bias : nullptr;
   a.bias_bh_stride = p.bias_bh_stride;
+  a.n_mirror = p.n_mirror;
+  for (int mi = 0; mi < kMaxMirrors; ++mi) a.mirror[mi] = mi < p.n_mirror ? p.mirror[mi] : nullptr;
   a.pairs = p.mode == 1 ? p.pairs : nullptr;
   if (p.nb > 0) {
     const int last_len = kv.tokens - 64 * (p.nb - 1);

@@ -80,6 +80,11 @@ cudaError_t run_stats(const b2_view* q, const b2_view* k, const b2_view* v, int 
                       h_half, partial, st);
 }
 
+void set_mirrors(AttnParams& p, char* const* mirrors, int n) {
+  p.n_mirror = n;
+  for (int i = 0; i < kMaxMirrors; ++i) p.mirror[i] = i < n ? mirrors[i] : nullptr;
+}
+
 cudaError_t run_attention(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* o, const AttnParams& p,
                           cudaStream_t st) {
   // D = 32 / 64 full and fixed-block attention keep the warp-MMA kernel,
@@ -100,7 +105,8 @@ cudaError_t run_attention(const b2_view* q, const b2_view* k, const b2_view* v, 
       }
     }
   }
-  if (!mma_native || (p.mode == 1 && q->head_dim != 128)) return cudaErrorNotSupported;
+  // only the tcgen05 kernel writes peer copies of the output
+  if (!mma_native || (p.mode == 1 && q->head_dim != 128) || p.n_mirror > 0) return cudaErrorNotSupported;
   g_last_kernel = "mma_sync";
   return launch_attn_mma(p, q->dtype, q->batch * q->heads, st);
 }
@@ -442,9 +448,14 @@ int b2_pisa_workspace_layout(int32_t batch_heads, int32_t tokens, int32_t head_d
   return ok();
 }
 
-int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, int32_t exact_blocks,
-                    float scale, int32_t sink_block, int32_t stats_mode, int32_t first_order, void* workspace,
-                    void* stream) {
+}  // extern "C"
+
+namespace {
+// b2_pisa_forward, optionally storing every output row into n_mirror peer
+// copies of the output buffer as well (b2_pisa_forward_mirrored).
+int pisa_forward_impl(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, int32_t exact_blocks,
+                      float scale, int32_t sink_block, int32_t stats_mode, int32_t first_order, void* workspace,
+                      void* stream, char* const* mirrors, int n_mirror) {
   int rc = check_qkv_o(q, k, v, out, true);
   if (rc) return rc;
   if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA supports bfloat16 and float16");
@@ -467,6 +478,7 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
   if (exact_blocks == nb) {
     AttnParams p = base_params(q, k, v, out, scale);
     p.mode = 0;
+    set_mirrors(p, mirrors, n_mirror);
     err = run_attention(q, k, v, out, p, st);
     if (err != cudaSuccess) return cuda_fail(err, "dense attention launch");
     return ok();
@@ -504,9 +516,49 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
   p.vc = w.vc16;
   p.h = first_order ? w.h16 : nullptr;
   p.corr_scale = scale / static_cast<float>(q->tokens);
+  set_mirrors(p, mirrors, n_mirror);
   err = run_attention(q, k, v, out, p, st);
   if (err != cudaSuccess) return cuda_fail(err, "PISA attention launch");
   return ok();
+}
+}  // namespace
+
+extern "C" {
+
+int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, int32_t exact_blocks,
+                    float scale, int32_t sink_block, int32_t stats_mode, int32_t first_order, void* workspace,
+                    void* stream) {
+  return pisa_forward_impl(q, k, v, out, exact_blocks, scale, sink_block, stats_mode, first_order, workspace, stream,
+                           nullptr, 0);
+}
+
+int b2_pisa_forward_mirrored(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out,
+                             int32_t exact_blocks, float scale, int32_t sink_block, int32_t stats_mode,
+                             int32_t first_order, const void* out_buffer, int64_t out_buffer_bytes,
+                             void* const* mirrors, int32_t n_mirrors, void* workspace, void* stream) {
+  if (n_mirrors < 0 || n_mirrors > kMaxMirrors) return fail(B2_ERR_INVALID, "n_mirrors must be in [0,%d]", kMaxMirrors);
+  if (n_mirrors > 0 && mirrors == nullptr) return fail(B2_ERR_INVALID, "mirrors must be non-NULL");
+  int rc = check_view(out, "out");
+  if (rc) return rc;
+  // every row the kernel stores must lie inside [out_buffer, out_buffer + bytes):
+  // the same offsets are then inside each peer's buffer of that size
+  const int64_t es = esize_of(out->dtype);
+  const char* lo_addr = static_cast<const char*>(out->base);
+  const int64_t last = (int64_t(out->batch) - 1) * out->stride_b + (int64_t(out->heads) - 1) * out->stride_h +
+                       (int64_t(out->tokens) - 1) * out->stride_t + out->head_dim;
+  if (out_buffer == nullptr || out_buffer_bytes <= 0 || out->stride_b < 0 || out->stride_h < 0 || out->stride_t < 0 ||
+      lo_addr < static_cast<const char*>(out_buffer) ||
+      lo_addr + last * es > static_cast<const char*>(out_buffer) + out_buffer_bytes)
+    return fail(B2_ERR_INVALID, "out must lie inside [out_buffer, out_buffer + out_buffer_bytes)");
+  char* peer[kMaxMirrors] = {};
+  const int64_t off = lo_addr - static_cast<const char*>(out_buffer);
+  for (int i = 0; i < n_mirrors; ++i) {
+    if (mirrors[i] == nullptr || reinterpret_cast<uintptr_t>(mirrors[i]) % 16)
+      return fail(B2_ERR_INVALID, "mirror buffers must be non-NULL and 16-byte aligned");
+    peer[i] = static_cast<char*>(mirrors[i]) + off;
+  }
+  return pisa_forward_impl(q, k, v, out, exact_blocks, scale, sink_block, stats_mode, first_order, workspace, stream,
+                           peer, n_mirrors);
 }
 
 int b2_pisa_forward_spatial_host(const void* q_host, const void* k_host, const void* v_host, void* out_host,

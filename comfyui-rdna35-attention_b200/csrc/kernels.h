@@ -3,6 +3,7 @@
 #include "common.cuh"
 
 namespace b2 {
+constexpr int kMaxMirrors = 7;  // peer copies of an output (head-sharded calls over up to 8 GPUs)
 // Parameters of the fused attention kernel (see attn_mma.cu).
 struct AttnParams {
   Rows q, k, v, o;
@@ -24,6 +25,8 @@ struct AttnParams {
   int debug_withhold_q;  // diagnostics: never load Q, so the pipeline's bounded waits run out
   const float* bias;     // fixed-block masks: FP32 [BHm][T][64] additive terms, or NULL
   int64_t bias_bh_stride;  // elements between (batch, head) rows of bias; 0 = one mask for all
+  int n_mirror;            // peer copies of the output written with every row (tcgen05 kernel only)
+  char* mirror[kMaxMirrors];
   const int32_t* pairs;  // optional [BH][ceil(nq/2)][2] query-block pairing (-1: single)
 };
 // Arguments of the tcgen05 attention kernel (see attn_umma.cu).
@@ -47,6 +50,8 @@ struct UmmaArgs {
   int debug_withhold_q;  // diagnostics (b2_debug_withhold_q): Q is never loaded
   const float* bias;     // fixed-block mask terms (mode DIAG), see AttnParams
   int64_t bias_bh_stride;
+  int n_mirror;  // peer output copies, see AttnParams
+  char* mirror[kMaxMirrors];
 };
 bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const b2_view& o);
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,

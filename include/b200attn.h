@@ -214,6 +214,26 @@ int b2_pisa_workspace_layout(int32_t batch_heads, int32_t tokens,
                              int32_t head_dim, int32_t exact_blocks,
                              int64_t* offsets, int32_t n);
 
+/* ---- b2_pisa_forward for one rank of a head-sharded call (no counterpart in
+ * the reference, whose path runs on one device).  `out` is this rank's head
+ * slice inside the output buffer [out_buffer, out_buffer + out_buffer_bytes)
+ * (e.g. the BHTD view of columns [h0*D, h1*D) of a [B,T,H*D] raster); every
+ * output row is stored there and, in the same kernel epilogue, at the same
+ * byte offset inside each of the n_mirrors (<= 7) peer buffers mirrors[i],
+ * which are other GPUs' copies of that buffer mapped into this process
+ * (peer-to-peer stores over NVLink).  All ranks writing their slices this way
+ * assemble the full output on every GPU without a separate all-gather; the
+ * caller synchronises the ranks before reading it.  Rejects an `out` view
+ * that reaches outside the buffer.  tcgen05 path only (D = 128 views TMA can
+ * address); other requests fail with B2_ERR_CUDA. */
+int b2_pisa_forward_mirrored(const b2_view* q, const b2_view* k,
+                             const b2_view* v, const b2_view* out,
+                             int32_t exact_blocks, float scale,
+                             int32_t sink_block, int32_t stats_mode,
+                             int32_t first_order, const void* out_buffer,
+                             int64_t out_buffer_bytes, void* const* mirrors,
+                             int32_t n_mirrors, void* workspace, void* stream);
+
 /* ---- Pipelined PISA HYD forward from host memory.  No counterpart in the
  * reference (its forward_spatial_bhtd, rdna35_pisa_ck/__init__.py:406-433,
  * takes device tensors).  q/k/v_host and out_host: page-locked raster
