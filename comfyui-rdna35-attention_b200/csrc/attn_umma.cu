@@ -744,7 +744,16 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
             if (c0 + 8 * q4 < a.o.dim)
               dst[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
         }
-        if constexpr (MIRROR) {
+        if constexpr (MIRROR && NW == 1) {
+          // stage the row for the peer copies: 128 rows x 256 B in the (now
+          // idle) K ring, 16-byte chunks XOR-swizzled by the row
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int chunk = (c0 >> 3) + q4;
+            *reinterpret_cast<uint4*>(k_s + row * 256 + ((chunk ^ (row & 15)) << 4)) =
+                make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+          }
+        } else if constexpr (MIRROR) {
           // the same 16-byte stores into the other GPUs' copies of the output
           // buffer (peer memory over NVLink), at the same offset
           const int64_t off = (orow - a.o.base) + c0 * 2;
@@ -754,6 +763,25 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
             for (int q4 = 0; q4 < 4; ++q4)
               if (c0 + 8 * q4 < a.o.dim)
                 md[q4] = make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+          }
+        }
+      }
+    }
+    if constexpr (MIRROR && NW == 1) {
+      // peer copies with coalesced rows: a warp writes two whole 256-byte
+      // rows per instruction over NVLink
+      named_barrier_sync(1, 128);
+      const int tid = threadIdx.x - 64;
+      if (!*abort_flag) {
+        for (int i = tid; i < 128 * 16; i += 128) {
+          const int r = i >> 4;
+          const int ch = i & 15;
+          const int rh = r >> 6;
+          const int tq_r = (rh ? qb : qa) * 64 + (r & 63);
+          if ((rh == 0 || has_b) && tq_r < a.tq && ch * 8 < a.o.dim) {
+            const uint4 val = *reinterpret_cast<const uint4*>(k_s + r * 256 + ((ch ^ (r & 15)) << 4));
+            const int64_t off = (a.o.row(bh, tq_r) - a.o.base) + ch * 16;
+            for (int mi = 0; mi < a.n_mirror; ++mi) *reinterpret_cast<uint4*>(a.mirror[mi] + off) = val;
           }
         }
       }
