@@ -76,6 +76,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2_pisa_forward": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _I32, _F32, _I32, _I32, _I32, _VP, _VP]),
     "b2_pisa_forward_mirrored": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _I32, _F32, _I32, _I32, _I32, _VP,
                                                 _I64, ctypes.POINTER(_VP), _I32, _VP, _VP]),
+    "b2_pisa_forward_multicast": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _I32, _F32, _I32, _I32, _I32, _VP,
+                                                 _I64, _VP, _VP, _VP]),
     "b2_pisa_forward_spatial_host": (ctypes.c_int, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _I32, _I32, _I32,
                                                     _I32, _I32, _I32, _F32, _I32, _I32, _VP, _VP]),
     "b2_full_attention": (ctypes.c_int, [_VIEW_P, _VIEW_P, _VIEW_P, _VIEW_P, _F32, _VP, _VP]),

@@ -8,12 +8,15 @@ GPUs (one process per GPU, torch.distributed) therefore splits the heads
 into N contiguous ranges, each rank computing its range with the single-GPU
 kernels.  The outputs are exchanged in one of two ways:
 
-* ``exchange="peer"`` (default): the output lives in a symmetric buffer
-  (``torch.distributed._symmetric_memory``: every rank's copy mapped into
-  every process) and the attention kernel's epilogue stores each output row
-  both locally and into every peer's copy over NVLink
-  (``b2_pisa_forward_mirrored``), so the exchange overlaps the attention
-  itself; two device-side barriers bracket the call.
+* ``exchange="multicast"`` / ``"peer"``: the output lives in a symmetric
+  buffer (``torch.distributed._symmetric_memory``: every rank's copy mapped
+  into every process) and the attention kernel's epilogue, after its local
+  store, writes each output row (staged in shared memory, whole 256-byte
+  rows) either once through the buffer's NVLink multicast address, which the
+  NVSwitch replicates into every GPU's copy (``b2_pisa_forward_multicast``),
+  or into each peer's copy in turn (``b2_pisa_forward_mirrored``); two
+  device-side barriers bracket the call.  ``"auto"`` (default) takes
+  multicast where the buffer has a multicast mapping.
 * ``exchange="nccl"``: each rank computes into a local [B,T,Hs*D] buffer, one
   NCCL all-gather exchanges the shards and a 16-byte copy kernel interleaves
   the gathered [N,B,T,Hs*D] shards into the [B,T,H*D] raster.
@@ -96,21 +99,21 @@ def _symmetric_output(shape: tuple, dtype: torch.dtype, device: torch.device, gr
 
 def forward_spatial_bhtd_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_blocks: int,
                                  scale: float | None = None, sink_block: int | None = None, *, group=None,
-                                 out: torch.Tensor | None = None, exchange: str = "peer") -> torch.Tensor:
+                                 out: torch.Tensor | None = None, exchange: str = "auto") -> torch.Tensor:
     """Anima spatial PISA over the heads of all ranks of `group`.
 
     q/k/v: this rank's head shard, BHTD views [B,Hs,9216,128] of contiguous
     [B,9216,Hs,128] BF16 storage (heads head_range(H, N, rank) of the full
     call).  Returns the full [B,9216,N*Hs*128] raster output on every rank,
     equal to forward_spatial_bhtd over all H heads on one GPU.  With
-    exchange="peer" the returned tensor is the group's symmetric output
+    a symmetric-buffer exchange the returned tensor is the group's symmetric output
     buffer, valid until the next peer-exchange call of the same shape on the
     group (pass ``out`` to receive a copy instead)."""
     from . import (HEAD_DIM, SPATIAL_SIDE, _check_exact_and_sink, _checked_device, _float32,
                    _validate_spatial_bhtd, _workspace, forward_spatial_bhtd)
 
-    if exchange not in ("peer", "nccl"):
-        raise ValueError("exchange must be 'peer' or 'nccl'")
+    if exchange not in ("auto", "multicast", "peer", "nccl"):
+        raise ValueError("exchange must be 'auto', 'multicast', 'peer' or 'nccl'")
     world = dist.get_world_size(group)
     if exchange == "nccl" or world == 1:
         local = forward_spatial_bhtd(q, k, v, exact_blocks, scale=scale, sink_block=sink_block)
@@ -133,11 +136,18 @@ def forward_spatial_bhtd_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
     mirrors = (ctypes.c_void_p * len(peers))(*peers)
     ws = _workspace(q.device, batch * heads, tokens, exact_blocks) if exact_blocks < blocks else None
     scale_value = _float32(1.0 / (HEAD_DIM ** 0.5) if scale is None else scale)
+    multicast = int(getattr(handle, "multicast_ptr", 0) or 0)
+    if exchange == "multicast" and not multicast:
+        raise ValueError("the symmetric output buffer has no multicast mapping on this system")
+    use_multicast = multicast != 0 and exchange in ("auto", "multicast")
     handle.barrier(channel=0)  # every rank is done with the buffer's previous contents
-    _lib.check(_lib.LIB.b2_pisa_forward_mirrored(
-        ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(ov), exact_blocks, scale_value,
-        -2 if sink_block is None else sink_block, _lib.STATS_HYD, 1, full.data_ptr(),
-        full.numel() * full.element_size(), mirrors, len(peers), _lib.ptr(ws), _lib.stream_of(q)))
+    common = (ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(ov), exact_blocks, scale_value,
+              -2 if sink_block is None else sink_block, _lib.STATS_HYD, 1, full.data_ptr(),
+              full.numel() * full.element_size())
+    if use_multicast:
+        _lib.check(_lib.LIB.b2_pisa_forward_multicast(*common, multicast, _lib.ptr(ws), _lib.stream_of(q)))
+    else:
+        _lib.check(_lib.LIB.b2_pisa_forward_mirrored(*common, mirrors, len(peers), _lib.ptr(ws), _lib.stream_of(q)))
     handle.barrier(channel=1)  # every rank's rows have landed in every copy
     if out is not None:
         out.copy_(full)

@@ -781,7 +781,10 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
           if ((rh == 0 || has_b) && tq_r < a.tq && ch * 8 < a.o.dim) {
             const uint4 val = *reinterpret_cast<const uint4*>(k_s + r * 256 + ((ch ^ (r & 15)) << 4));
             const int64_t off = (a.o.row(bh, tq_r) - a.o.base) + ch * 16;
-            for (int mi = 0; mi < a.n_mirror; ++mi) *reinterpret_cast<uint4*>(a.mirror[mi] + off) = val;
+            if (a.mirror_multicast)
+              multimem_st16(a.mirror[0] + off, val);
+            else
+              for (int mi = 0; mi < a.n_mirror; ++mi) *reinterpret_cast<uint4*>(a.mirror[mi] + off) = val;
           }
         }
       }
@@ -965,6 +968,9 @@ cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view
   a.bias = p.mode == 2 ? p.bias : nullptr;
   a.bias_bh_stride = p.bias_bh_stride;
   a.n_mirror = p.n_mirror;
+  a.mirror_multicast = p.mirror_multicast;
+  // multicast stores exist only on the staged (one-warpgroup) epilogue
+  if (p.mirror_multicast && attn_warpgroups() != 1) return cudaSuccess;
   for (int mi = 0; mi < kMaxMirrors; ++mi) a.mirror[mi] = mi < p.n_mirror ? p.mirror[mi] : nullptr;
   a.pairs = p.mode == 1 ? p.pairs : nullptr;
   if (p.nb > 0) {

@@ -80,8 +80,9 @@ cudaError_t run_stats(const b2_view* q, const b2_view* k, const b2_view* v, int 
                       h_half, partial, st);
 }
 
-void set_mirrors(AttnParams& p, char* const* mirrors, int n) {
+void set_mirrors(AttnParams& p, char* const* mirrors, int n, int multicast) {
   p.n_mirror = n;
+  p.mirror_multicast = multicast;
   for (int i = 0; i < kMaxMirrors; ++i) p.mirror[i] = i < n ? mirrors[i] : nullptr;
 }
 
@@ -455,7 +456,7 @@ namespace {
 // copies of the output buffer as well (b2_pisa_forward_mirrored).
 int pisa_forward_impl(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out, int32_t exact_blocks,
                       float scale, int32_t sink_block, int32_t stats_mode, int32_t first_order, void* workspace,
-                      void* stream, char* const* mirrors, int n_mirror) {
+                      void* stream, char* const* mirrors, int n_mirror, int multicast) {
   int rc = check_qkv_o(q, k, v, out, true);
   if (rc) return rc;
   if (q->dtype == B2_F32) return fail(B2_ERR_UNSUPPORTED, "PISA supports bfloat16 and float16");
@@ -478,7 +479,7 @@ int pisa_forward_impl(const b2_view* q, const b2_view* k, const b2_view* v, cons
   if (exact_blocks == nb) {
     AttnParams p = base_params(q, k, v, out, scale);
     p.mode = 0;
-    set_mirrors(p, mirrors, n_mirror);
+    set_mirrors(p, mirrors, n_mirror, multicast);
     err = run_attention(q, k, v, out, p, st);
     if (err != cudaSuccess) return cuda_fail(err, "dense attention launch");
     return ok();
@@ -516,7 +517,7 @@ int pisa_forward_impl(const b2_view* q, const b2_view* k, const b2_view* v, cons
   p.vc = w.vc16;
   p.h = first_order ? w.h16 : nullptr;
   p.corr_scale = scale / static_cast<float>(q->tokens);
-  set_mirrors(p, mirrors, n_mirror);
+  set_mirrors(p, mirrors, n_mirror, multicast);
   err = run_attention(q, k, v, out, p, st);
   if (err != cudaSuccess) return cuda_fail(err, "PISA attention launch");
   return ok();
@@ -529,19 +530,17 @@ int b2_pisa_forward(const b2_view* q, const b2_view* k, const b2_view* v, const 
                     float scale, int32_t sink_block, int32_t stats_mode, int32_t first_order, void* workspace,
                     void* stream) {
   return pisa_forward_impl(q, k, v, out, exact_blocks, scale, sink_block, stats_mode, first_order, workspace, stream,
-                           nullptr, 0);
+                           nullptr, 0, 0);
 }
 
-int b2_pisa_forward_mirrored(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out,
-                             int32_t exact_blocks, float scale, int32_t sink_block, int32_t stats_mode,
-                             int32_t first_order, const void* out_buffer, int64_t out_buffer_bytes,
-                             void* const* mirrors, int32_t n_mirrors, void* workspace, void* stream) {
-  if (n_mirrors < 0 || n_mirrors > kMaxMirrors) return fail(B2_ERR_INVALID, "n_mirrors must be in [0,%d]", kMaxMirrors);
-  if (n_mirrors > 0 && mirrors == nullptr) return fail(B2_ERR_INVALID, "mirrors must be non-NULL");
+}  // extern "C"
+
+namespace {
+// Every row a sharded call stores must lie inside [out_buffer, out_buffer +
+// bytes): the same offsets are then inside each peer's buffer of that size.
+int b2_pisa_forward_mirrored_checks(const b2_view* out, const void* out_buffer, int64_t out_buffer_bytes) {
   int rc = check_view(out, "out");
   if (rc) return rc;
-  // every row the kernel stores must lie inside [out_buffer, out_buffer + bytes):
-  // the same offsets are then inside each peer's buffer of that size
   const int64_t es = esize_of(out->dtype);
   const char* lo_addr = static_cast<const char*>(out->base);
   const int64_t last = (int64_t(out->batch) - 1) * out->stride_b + (int64_t(out->heads) - 1) * out->stride_h +
@@ -550,6 +549,21 @@ int b2_pisa_forward_mirrored(const b2_view* q, const b2_view* k, const b2_view* 
       lo_addr < static_cast<const char*>(out_buffer) ||
       lo_addr + last * es > static_cast<const char*>(out_buffer) + out_buffer_bytes)
     return fail(B2_ERR_INVALID, "out must lie inside [out_buffer, out_buffer + out_buffer_bytes)");
+  return B2_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int b2_pisa_forward_mirrored(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out,
+                             int32_t exact_blocks, float scale, int32_t sink_block, int32_t stats_mode,
+                             int32_t first_order, const void* out_buffer, int64_t out_buffer_bytes,
+                             void* const* mirrors, int32_t n_mirrors, void* workspace, void* stream) {
+  if (n_mirrors < 0 || n_mirrors > kMaxMirrors) return fail(B2_ERR_INVALID, "n_mirrors must be in [0,%d]", kMaxMirrors);
+  if (n_mirrors > 0 && mirrors == nullptr) return fail(B2_ERR_INVALID, "mirrors must be non-NULL");
+  int rc = b2_pisa_forward_mirrored_checks(out, out_buffer, out_buffer_bytes);
+  if (rc) return rc;
+  const char* lo_addr = static_cast<const char*>(out->base);
   char* peer[kMaxMirrors] = {};
   const int64_t off = lo_addr - static_cast<const char*>(out_buffer);
   for (int i = 0; i < n_mirrors; ++i) {
@@ -558,7 +572,22 @@ int b2_pisa_forward_mirrored(const b2_view* q, const b2_view* k, const b2_view* 
     peer[i] = static_cast<char*>(mirrors[i]) + off;
   }
   return pisa_forward_impl(q, k, v, out, exact_blocks, scale, sink_block, stats_mode, first_order, workspace, stream,
-                           peer, n_mirrors);
+                           peer, n_mirrors, 0);
+}
+
+int b2_pisa_forward_multicast(const b2_view* q, const b2_view* k, const b2_view* v, const b2_view* out,
+                              int32_t exact_blocks, float scale, int32_t sink_block, int32_t stats_mode,
+                              int32_t first_order, const void* out_buffer, int64_t out_buffer_bytes,
+                              void* multicast_buffer, void* workspace, void* stream) {
+  if (multicast_buffer == nullptr || reinterpret_cast<uintptr_t>(multicast_buffer) % 16)
+    return fail(B2_ERR_INVALID, "multicast_buffer must be non-NULL and 16-byte aligned");
+  void* const one[1] = {multicast_buffer};
+  // the same bounds checks and offset as the mirrored form
+  int rc = b2_pisa_forward_mirrored_checks(out, out_buffer, out_buffer_bytes);
+  if (rc) return rc;
+  char* mc = static_cast<char*>(one[0]) + (static_cast<const char*>(out->base) - static_cast<const char*>(out_buffer));
+  return pisa_forward_impl(q, k, v, out, exact_blocks, scale, sink_block, stats_mode, first_order, workspace, stream,
+                           &mc, 1, 1);
 }
 
 int b2_pisa_forward_spatial_host(const void* q_host, const void* k_host, const void* v_host, void* out_host,

@@ -27,6 +27,7 @@ struct AttnParams {
   int64_t bias_bh_stride;  // elements between (batch, head) rows of bias; 0 = one mask for all
   int n_mirror;            // peer copies of the output written with every row (tcgen05 kernel only)
   char* mirror[kMaxMirrors];
+  int mirror_multicast;    // 1: mirror[0] is a multicast address reaching every GPU's copy
   const int32_t* pairs;  // optional [BH][ceil(nq/2)][2] query-block pairing (-1: single)
 };
 // Arguments of the tcgen05 attention kernel (see attn_umma.cu).
@@ -52,6 +53,7 @@ struct UmmaArgs {
   int64_t bias_bh_stride;
   int n_mirror;  // peer output copies, see AttnParams
   char* mirror[kMaxMirrors];
+  int mirror_multicast;
 };
 bool umma_supported(const b2_view& q, const b2_view& k, const b2_view& v, const b2_view& o);
 cudaError_t launch_attn_umma(const b2_view& qv, const b2_view& kv, const b2_view& vv, const b2_view& ov,

@@ -103,6 +103,14 @@ static __device__ __noinline__ void drain_loads(uint64_t* full, int stages, int 
   if (extra != nullptr) mbar_wait(extra, 0, &no_abort, status, 31);
 }
 
+// One 16-byte store through a multicast address (NVLink SHARP): the switch
+// writes it into every GPU's copy of the buffer.
+__device__ __forceinline__ void multimem_st16(void* mc_addr, uint4 v) {
+  asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(mc_addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -234,6 +234,20 @@ int b2_pisa_forward_mirrored(const b2_view* q, const b2_view* k,
                              int64_t out_buffer_bytes, void* const* mirrors,
                              int32_t n_mirrors, void* workspace, void* stream);
 
+/* ---- b2_pisa_forward_mirrored with one multicast address instead of peer
+ * pointers (no counterpart in the reference): multicast_buffer is an NVLink
+ * multicast mapping of every GPU's copy of the output buffer (NVSwitch
+ * SHARP), so each output row is stored once (multimem.st) and the switch
+ * writes it into every copy, this GPU's included.  Same bounds checks;
+ * one-warpgroup tcgen05 layout only. */
+int b2_pisa_forward_multicast(const b2_view* q, const b2_view* k,
+                              const b2_view* v, const b2_view* out,
+                              int32_t exact_blocks, float scale,
+                              int32_t sink_block, int32_t stats_mode,
+                              int32_t first_order, const void* out_buffer,
+                              int64_t out_buffer_bytes, void* multicast_buffer,
+                              void* workspace, void* stream);
+
 /* ---- Pipelined PISA HYD forward from host memory.  No counterpart in the
  * reference (its forward_spatial_bhtd, rdna35_pisa_ck/__init__.py:406-433,
  * takes device tensors).  q/k/v_host and out_host: page-locked raster

@@ -1,7 +1,8 @@
 """One rank of the multi-GPU head-sharding check (run under torchrun by
 tests/test_gpu_multi.py): every rank computes its heads of the config-3
-call with the peer exchange and with the NCCL exchange, and rank 0 compares
-both with the single-GPU call over all heads, bit for bit."""
+call with the default exchange (multicast where available), the peer-store
+exchange and the NCCL exchange, and every result is compared with the
+single-GPU call over all heads, bit for bit."""
 import os
 import pathlib
 import sys
@@ -28,15 +29,19 @@ def main() -> int:
     shard = [x[:, h0:h1].permute(0, 2, 1, 3).contiguous().cuda().permute(0, 2, 1, 3) for x in (q, k, v)]
     ok = True
     for _ in range(2):  # twice: the symmetric buffer is reused
-        peer = forward_spatial_bhtd_sharded(*shard, 23).clone()
+        auto = forward_spatial_bhtd_sharded(*shard, 23).clone()
+        peer = forward_spatial_bhtd_sharded(*shard, 23, exchange="peer").clone()
         nccl = forward_spatial_bhtd_sharded(*shard, 23, exchange="nccl")
         torch.cuda.synchronize()
         full = [x.permute(0, 2, 1, 3).contiguous().cuda().permute(0, 2, 1, 3) for x in (q, k, v)]
         ref = b200_pisa.forward_spatial_bhtd(*full, 23)
-        ok = ok and torch.equal(peer, ref) and torch.equal(nccl, ref)
+        ok = ok and torch.equal(auto, ref) and torch.equal(peer, ref) and torch.equal(nccl, ref)
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
+        from b200_pisa import sharded
+        _, handle = next(iter(sharded._SYMMETRIC.values()))
+        print("multicast:", bool(getattr(handle, "multicast_ptr", 0)))
         print("SHARDED_OK" if flag.item() == 1 else "SHARDED_MISMATCH")
     dist.destroy_process_group()
     return 0 if flag.item() == 1 else 1
