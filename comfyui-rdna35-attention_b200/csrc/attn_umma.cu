@@ -257,12 +257,7 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
   const int bh = blockIdx.y;
   int qa = 2 * pair;
   int qb = 2 * pair + 1;
-  if (a.pairs != nullptr) {
-    qa = a.pairs[(int64_t(bh) * gridDim.x + pair) * 2];
-    qb = a.pairs[(int64_t(bh) * gridDim.x + pair) * 2 + 1];
-    if (qb < 0) qb = a.nqb;  // single block: half B inactive
-  }
-  const bool has_b = qb < a.nqb;
+  bool has_b = qb < a.nqb;  // the pairing kernel's output is read after grid_dep_wait
   const int ntail = a.nb > 0 ? (a.nb + 63) / 64 : 0;
   const int words = (a.nb + 31) >> 5;
 
@@ -312,6 +307,12 @@ attn_umma_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constan
   // launched with programmatic stream serialization: everything below reads
   // the routing results (or the inputs) and writes the output
   grid_dep_wait();
+  if (a.pairs != nullptr) {
+    qa = a.pairs[(int64_t(bh) * gridDim.x + pair) * 2];
+    qb = a.pairs[(int64_t(bh) * gridDim.x + pair) * 2 + 1];
+    if (qb < 0) qb = a.nqb;  // single block: half B inactive
+    has_b = qb < a.nqb;
+  }
   if (a.mode == 1 && warp == 0) {
     // union of the two query blocks' selected key blocks, sorted, each entry
     // tagged with the half(s) that selected it: the lanes OR the (clamped)
