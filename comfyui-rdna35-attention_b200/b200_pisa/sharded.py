@@ -34,6 +34,7 @@ import torch.distributed as dist
 from . import _lib
 
 _SYMMETRIC: dict = {}
+_SYMMETRIC_UNAVAILABLE: set = set()  # why the automatic exchange fell back to NCCL
 
 
 def head_range(heads: int, world: int, rank: int) -> tuple[int, int]:
@@ -126,7 +127,15 @@ def forward_spatial_bhtd_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
     _checked_device(q.device.index)
     if world - 1 > 7:
         raise ValueError("the peer exchange supports at most 8 ranks")
-    full, handle = _symmetric_output((batch, tokens, world * heads * dim), q.dtype, q.device, group)
+    try:
+        full, handle = _symmetric_output((batch, tokens, world * heads * dim), q.dtype, q.device, group)
+    except (RuntimeError, OSError) as exc:
+        if exchange != "auto":
+            raise
+        # no symmetric memory on this system (e.g. no peer access): NCCL exchange
+        _SYMMETRIC_UNAVAILABLE.add(str(exc)[:200])
+        local = forward_spatial_bhtd(q, k, v, exact_blocks, scale=scale, sink_block=sink_block)
+        return gather_head_shards(local, group=group, out=out)
     h0 = rank * heads
     local = full.view(batch, tokens, world * heads, dim)[:, :, h0:h0 + heads]
     tiled = dict(order=_lib.ORDER_TILED8, grid=(SPATIAL_SIDE, SPATIAL_SIDE))
