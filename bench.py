@@ -23,7 +23,8 @@ it is ``b200_pisa.forward_spatial_bhtd_host`` (the copies in and out are
 inside the timed region and overlap the compute of neighbouring head
 stages; the unstaged copy-in, call, copy-out time is reported beside it).
 On N GPUs each rank copies its heads' q/k/v in, runs the sharded call and
-copies the full gathered output out.
+copies its heads' columns of the output out (the job's input and output
+each cross PCIe once; the line gives per-rank and job byte counts).
 
 ``--impl reference`` times the reference's PyTorch HYD path restated on the
 host CPU (oracle/pisa_oracle.py, the batched form that mirrors the
@@ -286,14 +287,17 @@ def run_b200(args) -> None:
             b200_pisa.forward_spatial_bhtd_host(*host_bhtd, exact_blocks=EXACT, device=device, out=out_host,
                                                 heads_per_stage=args.heads_per_stage)
     else:
-        # this rank's heads in, sharded call with the all-gather, full output out
+        # this rank's heads in, sharded call (every rank then holds the full
+        # output), and this rank's share of the job's output back to the host:
+        # its heads' columns, so the job's result crosses PCIe once in total
         dev_bthd = [torch.empty_like(h, device=device) for h in host]
+        out_host = torch.empty((B, T, hs * D), dtype=torch.bfloat16).pin_memory()
 
         def e2e_step():
             for d_, h_ in zip(dev_bthd, host):
                 d_.copy_(h_, non_blocking=True)
             out = forward_spatial_bhtd_sharded(*(x.permute(0, 2, 1, 3) for x in dev_bthd), EXACT)
-            out_host.copy_(out, non_blocking=True)
+            out_host.copy_(out[:, :, h0 * D:h1 * D], non_blocking=True)
 
     for _ in range(2):
         e2e_step()
@@ -349,6 +353,8 @@ def run_b200(args) -> None:
             "clocks": clock_info,
             "e2e": {"value": round(job_value(world, e2e_ms), 2), "unit": UNIT,
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    **({"bytes_per_rank": True, "job_h2d_bytes_per_step": h2d * world,
+                        "job_d2h_bytes_per_step": d2h * world} if world > 1 else {}),
                     "api": "forward_spatial_bhtd_host" if world == 1 else "forward_spatial_bhtd_sharded",
                     **({"heads_per_stage": args.heads_per_stage, "unstaged_ms_per_step": round(serial_ms, 4)}
                        if world == 1 else {})},
