@@ -23,20 +23,47 @@ NATIVE_HEAD_DIM = 128  # the kernels' tile width; smaller heads are zero-filled 
 SPATIAL_BLOCK_EDGE = 8
 
 
-# ---- token tiling helpers (generic_pisa.py:17-52); torch reshapes, used by
-# callers that want block-major copies and by the tests of the tiling rule
+# ---- token tiling helpers (the reference's generic_pisa.py:17-52 names).
+# Block-major order of a frame of H x W tokens: 8x8 tiles in raster order of
+# the tiles, each tile's 64 tokens in raster order inside the tile.  Here the
+# order is an index map, applied with one gather (pack) or scatter (unpack)
+# along the token axis; the kernels read the same order in place through
+# strided views, so these copies serve callers that want block-major tensors.
+def _block_order(height: int, width: int, device=None) -> torch.Tensor:
+    """raster index of the token at each block-major position of one frame."""
+    if height % SPATIAL_BLOCK_EDGE or width % SPATIAL_BLOCK_EDGE:
+        raise ValueError("spatial grid sides must be multiples of 8")
+    e = SPATIAL_BLOCK_EDGE
+    pos = torch.arange(height * width, device=device)
+    tile, inner = pos // (e * e), pos % (e * e)
+    tiles_per_row = width // e
+    row = (tile // tiles_per_row) * e + inner // e
+    col = (tile % tiles_per_row) * e + inner % e
+    return row * width + col
+
+
+def _frames_order(frames: int, height: int, width: int, device=None) -> torch.Tensor:
+    frame = height * width
+    base = _block_order(height, width, device)
+    return (torch.arange(frames, device=device)[:, None] * frame + base[None]).reshape(-1)
+
+
+def _gather_tokens(tensor, order: torch.Tensor):
+    return tensor.index_select(-2, order.to(tensor.device)).contiguous()
+
+
+def _scatter_tokens(tensor, order: torch.Tensor):
+    out = torch.empty_like(tensor)
+    out[..., order.to(tensor.device), :] = tensor
+    return out
+
+
 def _pack_spatial_blocks_2d(tensor, height: int, width: int):
-    gh, gw = height // SPATIAL_BLOCK_EDGE, width // SPATIAL_BLOCK_EDGE
-    shaped = tensor.reshape(tensor.shape[0], tensor.shape[1], gh, SPATIAL_BLOCK_EDGE, gw, SPATIAL_BLOCK_EDGE,
-                            tensor.shape[-1])
-    return shaped.permute(0, 1, 2, 4, 3, 5, 6).reshape_as(tensor).contiguous()
+    return _gather_tokens(tensor, _block_order(height, width))
 
 
 def _unpack_spatial_blocks_2d(tensor, height: int, width: int):
-    gh, gw = height // SPATIAL_BLOCK_EDGE, width // SPATIAL_BLOCK_EDGE
-    shaped = tensor.reshape(tensor.shape[0], tensor.shape[1], gh, gw, SPATIAL_BLOCK_EDGE, SPATIAL_BLOCK_EDGE,
-                            tensor.shape[-1])
-    return shaped.permute(0, 1, 2, 4, 3, 5, 6).reshape_as(tensor).contiguous()
+    return _scatter_tokens(tensor, _block_order(height, width))
 
 
 def _pack_spatial_blocks(tensor, side: int):
@@ -47,24 +74,20 @@ def _unpack_spatial_blocks(tensor, side: int):
     return _unpack_spatial_blocks_2d(tensor, side, side)
 
 
-def _per_frame(tensor, grid_sizes):
+def _check_video(tensor, grid_sizes):
     frames, height, width = grid_sizes
-    batch, heads, tokens, head_dim = tensor.shape
-    if tokens != frames * height * width:
+    if tensor.shape[-2] != frames * height * width:
         raise ValueError("video token shape does not match grid_sizes")
-    return tensor.unflatten(2, (frames, height * width)).transpose(1, 2).flatten(0, 1), batch, frames
 
 
 def _pack_video_blocks(tensor, grid_sizes):
-    per_frame, batch, frames = _per_frame(tensor, grid_sizes)
-    packed = _pack_spatial_blocks_2d(per_frame, grid_sizes[1], grid_sizes[2])
-    return packed.unflatten(0, (batch, frames)).transpose(1, 2).flatten(2, 3)
+    _check_video(tensor, grid_sizes)
+    return _gather_tokens(tensor, _frames_order(*grid_sizes))
 
 
 def _unpack_video_blocks(tensor, grid_sizes):
-    per_frame, batch, frames = _per_frame(tensor, grid_sizes)
-    unpacked = _unpack_spatial_blocks_2d(per_frame, grid_sizes[1], grid_sizes[2])
-    return unpacked.unflatten(0, (batch, frames)).transpose(1, 2).flatten(2, 3)
+    _check_video(tensor, grid_sizes)
+    return _scatter_tokens(tensor, _frames_order(*grid_sizes))
 
 
 def generic_pisa_attention(q, k, v, *, exact_budget: float, scale: float | None = None, return_backend: bool = False,
@@ -104,6 +127,46 @@ def generic_pisa_attention(q, k, v, *, exact_budget: float, scale: float | None 
     return (output, backend) if return_backend else output
 
 
+# Call-level reject ladder of the generic override: (check, reason) rows in
+# order, the first failing row names the reason (reason strings kept from
+# the reference's generic override).
+_CALL_LADDER = (
+    (lambda q, k, v, mask, dev, kw: kw.get("is_self_attention") is True, "not_explicit_self_attention"),
+    (lambda q, k, v, mask, dev, kw: not kw.get("is_kv_cached_attention", False), "kv_cached_attention_is_not_supported"),
+    (lambda q, k, v, mask, dev, kw: mask is None, "attention_mask_is_not_supported"),
+    (lambda q, k, v, mask, dev, kw: not kw.get("enable_gqa", False), "gqa_is_not_supported"),
+    (lambda q, k, v, mask, dev, kw: all(isinstance(t, torch.Tensor) for t in (q, k, v)), "qkv_are_not_tensors"),
+    (lambda q, k, v, mask, dev, kw: q.device.type == "cuda" and q.device.index == dev,
+     "validated_b200_device_is_required"),
+    (lambda q, k, v, mask, dev, kw: k.device == q.device == v.device, "qkv_must_share_one_device"),
+    (lambda q, k, v, mask, dev, kw: q.dtype in (torch.float16, torch.bfloat16) and k.dtype == q.dtype == v.dtype,
+     "matching_fp16_or_bf16_qkv_are_required"),
+)
+
+
+def _call_reject_reason(q, k, v, mask, device_index, kwargs) -> str | None:
+    for holds, reason in _CALL_LADDER:
+        if not holds(q, k, v, mask, device_index, kwargs):
+            return reason
+    return None
+
+
+def _bhtd_layout(q, k, v, heads, skip_reshape):
+    """((q, k, v) as [B,H,T,D] views, (B, T, D)) of ComfyUI's two input
+    layouts, or the reject reason when the tensors do not fit the layout."""
+    if skip_reshape:  # [B,H,T,D]
+        if q.ndim != 4 or not (q.shape == k.shape == v.shape):
+            return "matching_bhtd_qkv_are_required"
+        if q.shape[1] != heads:
+            return "head_count_mismatch"
+        return (q, k, v), (q.shape[0], q.shape[2], q.shape[3])
+    if q.ndim != 3 or not (q.shape == k.shape == v.shape) or q.shape[-1] % heads:  # [B,T,H*D]
+        return "matching_btc_qkv_divisible_by_heads_are_required"
+    batch, tokens, channels = q.shape
+    head_dim = channels // heads
+    return tuple(t.unflatten(2, (heads, head_dim)).transpose(1, 2) for t in (q, k, v)), (batch, tokens, head_dim)
+
+
 def make_generic_pisa_override(*, exact_budget: float, device_index: int, previous_override: Callable | None,
                                runtime_state, validate_output: bool = False) -> Callable:
     def fallback(original_func, *args, **kwargs):
@@ -119,42 +182,15 @@ def make_generic_pisa_override(*, exact_budget: float, device_index: int, previo
         block = options.get("block")
         block_index = options.get("block_index", 0)
         context = f"{block[0]}:{block[1]}:{block_index}" if isinstance(block, (tuple, list)) and len(block) == 2 else None
-        reason = None
-        if kwargs.get("is_self_attention") is not True:
-            reason = "not_explicit_self_attention"
-        elif kwargs.get("is_kv_cached_attention", False):
-            reason = "kv_cached_attention_is_not_supported"
-        elif mask is not None:
-            reason = "attention_mask_is_not_supported"
-        elif kwargs.get("enable_gqa", False):
-            reason = "gqa_is_not_supported"
-        elif not all(isinstance(t, torch.Tensor) for t in (q, k, v)):
-            reason = "qkv_are_not_tensors"
-        elif q.device.type != "cuda" or q.device.index != device_index:
-            reason = "validated_b200_device_is_required"
-        elif k.device != q.device or v.device != q.device:
-            reason = "qkv_must_share_one_device"
-        elif q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype:
-            reason = "matching_fp16_or_bf16_qkv_are_required"
+        reason = _call_reject_reason(q, k, v, mask, device_index, kwargs)
         if reason is None:
-            if skip_reshape:
-                if q.ndim != 4 or q.shape != k.shape or q.shape != v.shape:
-                    reason = "matching_bhtd_qkv_are_required"
-                else:
-                    batch, actual_heads, tokens, head_dim = q.shape
-                    if actual_heads != heads:
-                        reason = "head_count_mismatch"
-                    else:
-                        q_bhtd, k_bhtd, v_bhtd = q, k, v
+            layout = _bhtd_layout(q, k, v, heads, skip_reshape)
+            if isinstance(layout, str):
+                reason = layout
             else:
-                if q.ndim != 3 or q.shape != k.shape or q.shape != v.shape or q.shape[-1] % heads:
-                    reason = "matching_btc_qkv_divisible_by_heads_are_required"
-                else:
-                    batch, tokens, channels = q.shape
-                    head_dim = channels // heads
-                    q_bhtd, k_bhtd, v_bhtd = (t.unflatten(2, (heads, head_dim)).transpose(1, 2) for t in (q, k, v))
-            if reason is None and tokens < MIN_TOKENS:
-                reason = f"tokens_{tokens}_below_{MIN_TOKENS}"
+                (q_bhtd, k_bhtd, v_bhtd), (batch, tokens, head_dim) = layout
+                if tokens < MIN_TOKENS:
+                    reason = f"tokens_{tokens}_below_{MIN_TOKENS}"
         shape = tuple(q.shape) if isinstance(q, torch.Tensor) and q.ndim >= 2 else None
         if reason is not None:
             runtime_state.record(is_self_attention=kwargs.get("is_self_attention"), shape=shape,
