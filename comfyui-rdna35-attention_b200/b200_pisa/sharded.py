@@ -15,8 +15,9 @@ kernels.  The outputs are exchanged in one of two ways:
   rows) either once through the buffer's NVLink multicast address, which the
   NVSwitch replicates into every GPU's copy (``b2_pisa_forward_multicast``),
   or into each peer's copy in turn (``b2_pisa_forward_mirrored``); two
-  device-side barriers bracket the call.  ``"auto"`` (default) takes
-  multicast where the buffer has a multicast mapping.
+  device-side barriers bracket the call.  ``"auto"`` (default) uses the
+  peer stores: measured on 8 GPUs, 0.259 ms per call against 0.275 ms with
+  multicast (2 GPUs: 0.381 / 0.378 ms).
 * ``exchange="nccl"``: each rank computes into a local [B,T,Hs*D] buffer, one
   NCCL all-gather exchanges the shards and a 16-byte copy kernel interleaves
   the gathered [N,B,T,Hs*D] shards into the [B,T,H*D] raster.
@@ -148,7 +149,7 @@ def forward_spatial_bhtd_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
     multicast = int(getattr(handle, "multicast_ptr", 0) or 0)
     if exchange == "multicast" and not multicast:
         raise ValueError("the symmetric output buffer has no multicast mapping on this system")
-    use_multicast = multicast != 0 and exchange in ("auto", "multicast")
+    use_multicast = multicast != 0 and exchange == "multicast"
     handle.barrier(channel=0)  # every rank is done with the buffer's previous contents
     common = (ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(ov), exact_blocks, scale_value,
               -2 if sink_block is None else sink_block, _lib.STATS_HYD, 1, full.data_ptr(),

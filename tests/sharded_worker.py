@@ -1,7 +1,7 @@
 """One rank of the multi-GPU head-sharding check (run under torchrun by
 tests/test_gpu_multi.py): every rank computes its heads of the config-3
-call with the default exchange (multicast where available), the peer-store
-exchange and the NCCL exchange, and every result is compared with the
+call with the default (peer-store) exchange, the multicast exchange where
+the system offers it, and the NCCL exchange, and every result is compared with the
 single-GPU call over all heads, bit for bit."""
 import os
 import pathlib
@@ -13,6 +13,12 @@ import torch.distributed as dist
 ROOT = pathlib.Path(__file__).resolve().parents[1]
 for p in (ROOT / "comfyui-rdna35-attention_b200", ROOT / "oracle"):
     sys.path.insert(0, str(p))
+
+
+def has_multicast() -> bool:
+    from b200_pisa import sharded
+
+    return any(getattr(h, "multicast_ptr", 0) for _, h in sharded._SYMMETRIC.values())
 
 
 def main() -> int:
@@ -30,12 +36,13 @@ def main() -> int:
     ok = True
     for _ in range(2):  # twice: the symmetric buffer is reused
         auto = forward_spatial_bhtd_sharded(*shard, 23).clone()
+        multi = forward_spatial_bhtd_sharded(*shard, 23, exchange="multicast").clone() if has_multicast() else auto
         peer = forward_spatial_bhtd_sharded(*shard, 23, exchange="peer").clone()
         nccl = forward_spatial_bhtd_sharded(*shard, 23, exchange="nccl")
         torch.cuda.synchronize()
         full = [x.permute(0, 2, 1, 3).contiguous().cuda().permute(0, 2, 1, 3) for x in (q, k, v)]
         ref = b200_pisa.forward_spatial_bhtd(*full, 23)
-        ok = ok and torch.equal(auto, ref) and torch.equal(peer, ref) and torch.equal(nccl, ref)
+        ok = ok and torch.equal(auto, ref) and torch.equal(multi, ref) and torch.equal(peer, ref) and torch.equal(nccl, ref)
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
