@@ -127,3 +127,51 @@ def test_noalloc_statistics_share_the_view_checks():
     assert lib.b2_pisa_block_stats_noalloc(ctypes.byref(good), ctypes.byref(good), ctypes.byref(good),
                                            _lib.STATS_HYD, None, fake, fake, fake, None, None,
                                            None) == _lib.B2_ERR_INVALID
+
+
+def test_sharded_and_mask_entry_points_check_arguments_without_a_gpu():
+    """Host-side checks of the newer entry points fail before any launch:
+    output views outside the output buffer, bad mirror / multicast pointers,
+    mask arguments; and the workspace layout offsets are ordered and fit."""
+    import torch
+    from b200_pisa import _lib
+
+    lib = _lib.LIB
+    x = torch.zeros((1, 2, 64, 128), dtype=torch.bfloat16)
+    v = _lib.view(x)
+    fake = ctypes.c_void_p(4096)
+    buf = x.data_ptr()
+    nbytes = x.numel() * 2
+    peers = (ctypes.c_void_p * 1)(ctypes.c_void_p(1 << 20))
+    fwd = lib.b2_pisa_forward_mirrored
+    # the view reaches one byte past the buffer
+    assert fwd(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), 0, 0.1, -2, 0, 1, buf,
+               nbytes - 1, peers, 1, fake, None) == _lib.B2_ERR_INVALID
+    assert b"out_buffer" in lib.b2_last_error()
+    # the view starts before the buffer
+    assert fwd(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), 0, 0.1, -2, 0, 1, buf + 16,
+               nbytes, peers, 1, fake, None) == _lib.B2_ERR_INVALID
+    # too many mirrors, a misaligned mirror
+    assert fwd(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), 0, 0.1, -2, 0, 1, buf, nbytes,
+               peers, 8, fake, None) == _lib.B2_ERR_INVALID
+    bad_peer = (ctypes.c_void_p * 1)(ctypes.c_void_p((1 << 20) + 8))
+    assert fwd(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), 0, 0.1, -2, 0, 1, buf, nbytes,
+               bad_peer, 1, fake, None) == _lib.B2_ERR_INVALID
+    assert lib.b2_pisa_forward_multicast(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), 0, 0.1,
+                                         -2, 0, 1, buf, nbytes, None, fake, None) == _lib.B2_ERR_INVALID
+    # masks: unknown dtype, negative stride, misaligned bias
+    pack = lib.b2_pack_block_bias
+    assert pack(fake, 9, 0, 64, 1, 1, 64, fake, None) == _lib.B2_ERR_INVALID
+    assert pack(fake, 0, -1, 64, 1, 1, 64, fake, None) == _lib.B2_ERR_INVALID
+    assert pack(fake, 0, 0, 64, 1, 1, 64, ctypes.c_void_p(4100), None) == _lib.B2_ERR_INVALID
+    masked = lib.b2_fixed_block_attention_masked
+    assert masked(ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), ctypes.byref(v), 0.1, 0, ctypes.c_void_p(4100),
+                  0, None) == _lib.B2_ERR_INVALID
+    # workspace layout: ascending offsets inside b2_pisa_workspace_bytes
+    offs = (ctypes.c_int64 * _lib.WS_FIELDS)()
+    assert lib.b2_pisa_workspace_layout(32, 9216, 128, 23, offs, _lib.WS_FIELDS) == 0
+    total = lib.b2_pisa_workspace_bytes(32, 9216, 128, 23)
+    values = list(offs)
+    assert values == sorted(values) and values[0] == 0 and values[-1] < total
+    assert all(o % 256 == 0 for o in values)
+    assert lib.b2_pisa_workspace_layout(32, 9216, 64, 23, offs, _lib.WS_FIELDS) == _lib.B2_ERR_INVALID
