@@ -156,3 +156,30 @@ def test_config5_generic_pisa_video_full_shape(pisa):
     assert int((mismatched & ~ties).sum()) == 0
     exp, _ = oracle.generic_forward_batched(qs, ks, vs, exact, scale)
     torch.testing.assert_close(out[sample].float(), exp.float(), **TOL)
+
+
+@pytest.mark.parametrize("sink", [0, -1])
+def test_config3_sink_block_index_sets_and_output(pisa, sink):
+    """The forced sink block (first or last key block always exact) at the
+    full Anima size: routed sets contain the sink on every row and match the
+    oracle's outside the near-tie window; outputs within the BF16 gate."""
+    q, k, v = oracle.anima_inputs(batch=1, heads=4, seed=40 + sink)
+    out, idx, h_norm = pisa.forward_spatial_bhtd_with_routing(*(to_dev_bhtd(x) for x in (q, k, v)), exact_blocks=23,
+                                                              sink_block=sink)
+    torch.cuda.synchronize()
+    idx, h_norm, out = idx.cpu().long(), h_norm.cpu(), out.cpu()
+    packed = [oracle.pack_spatial(x) for x in (q, k, v)]
+    stats = oracle.hyd_block_stats(*packed)
+    qc, kc, _, _, hn_ref = stats
+    scale = float(torch.tensor(1.0 / math.sqrt(128), dtype=torch.float32))
+    scores = oracle.route_scores_hyd(qc, kc, hn_ref, scale)
+    ref_idx = oracle.select_topk(scores, 23, sink_block=sink)
+    sink_index = 143 if sink == -1 else 0
+    assert bool((idx == sink_index).any(-1).all())
+    forced = scores.clone()
+    forced[..., sink_index] = torch.inf
+    d_log = (torch.log(h_norm + 1e-5) - torch.log(hn_ref + 1e-5)).abs().max().item()
+    ties = oracle.near_tie_rows(forced, 23, abs_tol=2 * (d_log + _score_error_bound(qc, kc, scale)))
+    assert int(((idx != ref_idx).any(-1) & ~ties).sum()) == 0
+    exp, _ = oracle.hyd_forward_batched(*packed, 23, sink_block=sink, stats=stats)
+    torch.testing.assert_close(out.float(), oracle.unpack_spatial(exp, 1, 4).float(), **TOL)
